@@ -1,0 +1,591 @@
+// Kernel (a): shared-prefix (level-1) verify attention on sm_100a.
+//
+// Replaces flashinfer.single_prefill_with_kv_cache(q_all, k_shared, v_shared,
+// causal=False, return_lse=True, sm_scale) at generation/verification.py:145-148
+// and model/dflash.py:112-115: every query row (all branches x block tokens x
+// the G query heads of a kv head) attends the whole shared prefix of its kv
+// head. Output convention (FlashInfer's, include/flashinfer/attention/state.cuh):
+// normalised O plus the base-2 log-sum-exp lse = m + log2(sum 2^(s*scale*log2e - m)).
+//
+// Design (one persistent CTA per SM, plan_layout.h for the work partition):
+//   warp 8      TMA producer: Q tile pair once per item; per 128-key tile one
+//               2 KB box per page per 64-column panel for K and for V, straight
+//               from the paged cache (no transpose copy), 128-byte swizzle.
+//   warp 9      MMA issuer (one thread): S_i = Q_i K^T (tcgen05.mma, smem x smem
+//               -> TMEM, M=128 N=128 K=16 steps) and O_i += P_i V (A operand =
+//               P_i in TMEM, B = V in smem, MN-major).
+//   warps 0-7   two softmax warpgroups, one per 128-row query tile; thread =
+//               row = TMEM lane. Online softmax in the log2 domain with a lazy
+//               max (O is rescaled in TMEM only when the running max grows by
+//               more than 8, i.e. a factor 256, which keeps p <= 256 in bf16).
+// TMEM: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D); P_i is written
+// as packed bf16 over the first 64 columns of S_i.
+// The two tiles ping-pong: while warpgroup 0 turns S0 into P0 the tensor core
+// runs Q1 K^T and P1 V, and vice versa.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "plan_layout.h"
+
+namespace d2sd {
+namespace {
+
+using namespace plan;
+
+constexpr int kNumThreads = 320;
+constexpr int kTmaWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 bytes (64 bf16)
+constexpr uint32_t kTmemCols = 512;
+
+template <int D>
+struct Cfg {
+  static constexpr int kPanels = D / 64;
+  static constexpr int kTileBytes = 128 * D * 2;  // a 128-row Q tile or 128-key K/V tile
+  static constexpr int kStages = (D == 128) ? 2 : 4;
+  static constexpr int kSmemQ = 0;
+  static constexpr int kSmemK = kSmemQ + 2 * kTileBytes;
+  static constexpr int kSmemV = kSmemK + kStages * kTileBytes;
+  static constexpr int kSmemBar = kSmemV + kStages * kTileBytes;
+  // barrier indices
+  static constexpr int B_QFULL = 0;
+  static constexpr int B_QFREE = 1;
+  static constexpr int B_KFULL = 2;
+  static constexpr int B_VFULL = B_KFULL + kStages;
+  static constexpr int B_KVEMPTY = B_VFULL + kStages;
+  static constexpr int B_SFULL = B_KVEMPTY + kStages;
+  static constexpr int B_PFULL = B_SFULL + 2;
+  static constexpr int B_OFINAL = B_PFULL + 2;
+  static constexpr int B_OFREE = B_OFINAL + 2;
+  static constexpr int kNumBars = B_OFREE + 2;
+  static constexpr int kSmemBytes = kSmemBar + kNumBars * 8 + 16 + 1024;  // + align slack
+  static constexpr int kSlotFloats = kTileRows * (D + 1);
+};
+
+struct PrefixParams {
+  const int32_t* plan;
+  const int32_t* page_table;         // nullptr: contiguous KV
+  const int32_t* page_table_offset;  // per request
+  float* partial;
+  int32_t* status;
+  int32_t rows_per_box;  // page_size (paged) or 16 (contiguous)
+  int32_t G;
+  float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t s_col(int i) { return static_cast<uint32_t>(i * 128); }
+__device__ __forceinline__ uint32_t o_col(int i) { return static_cast<uint32_t>(256 + i * 128); }
+
+// Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) {
+    // the phase has completed and cannot advance without this warp, so every
+    // lane's own acquire of it succeeds at once
+    while (!mbar_try_wait(bar, parity)) {
+    }
+  }
+  return ok != 0;
+}
+
+template <int D>
+__device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                         const PrefixParams& p, uint8_t* smem, uint64_t* bars, volatile int* abort,
+                         int item_begin, int item_end) {
+  using C = Cfg<D>;
+  const int32_t* items = p.plan + p.plan[H_OFF_ITEMS];
+  const int G = p.G;
+  const int rpb = p.rows_per_box;
+  const int boxes = kTileKeys / rpb;
+  uint32_t kt = 0;
+  for (int it = item_begin; it < item_end; ++it) {
+    const int32_t* I = items + it * kItemInts;
+    const int r = I[I_REQ], h = I[I_HEAD], t0 = I[I_T0], t1 = I[I_T1];
+    const int kv_end = I[I_KV_END], qtok = I[I_QTOK];
+    if (it > item_begin) {
+      if (!mbar_wait(&bars[C::B_QFREE], (it - item_begin - 1) & 1, abort)) return;
+    }
+    mbar_arrive_expect_tx(&bars[C::B_QFULL], 2 * C::kTileBytes);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+#pragma unroll
+      for (int pn = 0; pn < C::kPanels; ++pn) {
+        tma_load_3d(smem + C::kSmemQ + i * C::kTileBytes + pn * kPanelBytes, tm_q,
+                    &bars[C::B_QFULL], pn * 64, h * G, qtok + i * (kTileRows / G));
+      }
+    }
+    const int base = p.page_table_offset ? p.page_table_offset[r] : 0;
+    const int last_page = (kv_end - 1) / rpb;
+    for (int t = t0; t < t1; ++t, ++kt) {
+      const int s = static_cast<int>(kt % C::kStages);
+      const uint32_t use = kt / C::kStages;
+      if (use > 0) {
+        if (!mbar_wait(&bars[C::B_KVEMPTY + s], (use - 1) & 1, abort)) return;
+      }
+      uint8_t* ks = smem + C::kSmemK + s * C::kTileBytes;
+      uint8_t* vs = smem + C::kSmemV + s * C::kTileBytes;
+      mbar_arrive_expect_tx(&bars[C::B_KFULL + s], C::kTileBytes);
+      for (int b = 0; b < boxes; ++b) {
+        const int pos0 = t * kTileKeys + b * rpb;
+        int c1, c3;
+        if (p.page_table) {
+          int pg = pos0 / rpb;
+          if (pg > last_page) pg = last_page;  // finite filler, masked in softmax
+          c1 = 0;
+          c3 = p.page_table[base + pg];
+        } else {
+          c1 = base + pos0;
+          c3 = 0;
+        }
+#pragma unroll
+        for (int pn = 0; pn < C::kPanels; ++pn)
+          tma_load_4d(ks + pn * kPanelBytes + b * rpb * 128, tm_k, &bars[C::B_KFULL + s], pn * 64,
+                      c1, h, c3);
+      }
+      mbar_arrive_expect_tx(&bars[C::B_VFULL + s], C::kTileBytes);
+      for (int b = 0; b < boxes; ++b) {
+        const int pos0 = t * kTileKeys + b * rpb;
+        int c1, c3;
+        if (p.page_table) {
+          int pg = pos0 / rpb;
+          if (pg > last_page) pg = last_page;
+          c1 = 0;
+          c3 = p.page_table[base + pg];
+        } else {
+          c1 = base + pos0;
+          c3 = 0;
+        }
+#pragma unroll
+        for (int pn = 0; pn < C::kPanels; ++pn)
+          tma_load_4d(vs + pn * kPanelBytes + b * rpb * 128, tm_v, &bars[C::B_VFULL + s], pn * 64,
+                      c1, h, c3);
+      }
+    }
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void issue_qk(uint32_t tmem, int i, uint8_t* smem, int stage) {
+  using C = Cfg<D>;
+  constexpr uint32_t idesc = umma_idesc_bf16(128, 128, false);
+  const uint32_t a0 = smem_u32(smem + C::kSmemQ + i * C::kTileBytes);
+  const uint32_t b0 = smem_u32(smem + C::kSmemK + stage * C::kTileBytes);
+#pragma unroll
+  for (int ks = 0; ks < D / 16; ++ks) {
+    const uint32_t off = (ks / 4) * kPanelBytes + (ks % 4) * 32;
+    umma_ss(tmem + s_col(i), umma_desc_sw128(a0 + off, 16, 1024), umma_desc_sw128(b0 + off, 16, 1024),
+            idesc, ks > 0 ? 1u : 0u);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void issue_pv(uint32_t tmem, int i, uint8_t* smem, int stage,
+                                         bool accumulate) {
+  using C = Cfg<D>;
+  constexpr uint32_t idesc = umma_idesc_bf16(128, D, true);
+  const uint32_t b0 = smem_u32(smem + C::kSmemV + stage * C::kTileBytes);
+#pragma unroll
+  for (int ks = 0; ks < kTileKeys / 16; ++ks) {
+    umma_ts(tmem + o_col(i), tmem + s_col(i) + ks * 8,
+            umma_desc_sw128(b0 + ks * 16 * 128, kPanelBytes, 1024), idesc,
+            (accumulate || ks > 0) ? 1u : 0u);
+  }
+}
+
+template <int D>
+__device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars, uint32_t tmem,
+                           volatile int* abort, int item_begin, int item_end) {
+  using C = Cfg<D>;
+  const int32_t* items = p.plan + p.plan[H_OFF_ITEMS];
+  uint32_t kt = 0;
+  uint32_t pcount[2] = {0, 0};
+  for (int it = item_begin; it < item_end; ++it) {
+    const int k = it - item_begin;
+    const int32_t* I = items + it * kItemInts;
+    const int n = I[I_T1] - I[I_T0];
+    if (!mbar_wait(&bars[C::B_QFULL], k & 1, abort)) return;
+    tc_fence_after();
+    {
+      const int s = static_cast<int>(kt % C::kStages);
+      if (!mbar_wait(&bars[C::B_KFULL + s], (kt / C::kStages) & 1, abort)) return;
+      tc_fence_after();
+      issue_qk<D>(tmem, 0, smem, s);
+      umma_commit(&bars[C::B_SFULL + 0]);
+      issue_qk<D>(tmem, 1, smem, s);
+      umma_commit(&bars[C::B_SFULL + 1]);
+      if (n == 1) umma_commit(&bars[C::B_QFREE]);
+    }
+    for (int j = 0; j < n; ++j) {
+      const uint32_t cur = kt + j;
+      const int s = static_cast<int>(cur % C::kStages);
+      const bool has_next = j + 1 < n;
+      const int sn = static_cast<int>((cur + 1) % C::kStages);
+      if (!mbar_wait(&bars[C::B_VFULL + s], (cur / C::kStages) & 1, abort)) return;
+      // ---- tile 0 ----
+      if (j == 0 && k > 0) {
+        if (!mbar_wait(&bars[C::B_OFREE + 0], (k - 1) & 1, abort)) return;
+      }
+      if (!mbar_wait(&bars[C::B_PFULL + 0], pcount[0] & 1, abort)) return;
+      ++pcount[0];
+      tc_fence_after();
+      issue_pv<D>(tmem, 0, smem, s, j > 0);
+      if (has_next) {
+        if (!mbar_wait(&bars[C::B_KFULL + sn], ((cur + 1) / C::kStages) & 1, abort)) return;
+        tc_fence_after();
+        issue_qk<D>(tmem, 0, smem, sn);
+        umma_commit(&bars[C::B_SFULL + 0]);
+      }
+      // ---- tile 1 ----
+      if (j == 0 && k > 0) {
+        if (!mbar_wait(&bars[C::B_OFREE + 1], (k - 1) & 1, abort)) return;
+      }
+      if (!mbar_wait(&bars[C::B_PFULL + 1], pcount[1] & 1, abort)) return;
+      ++pcount[1];
+      tc_fence_after();
+      issue_pv<D>(tmem, 1, smem, s, j > 0);
+      umma_commit(&bars[C::B_KVEMPTY + s]);
+      if (has_next) {
+        issue_qk<D>(tmem, 1, smem, sn);
+        umma_commit(&bars[C::B_SFULL + 1]);
+        if (j + 2 == n) umma_commit(&bars[C::B_QFREE]);
+      }
+    }
+    umma_commit(&bars[C::B_OFINAL + 0]);
+    umma_commit(&bars[C::B_OFINAL + 1]);
+    kt += n;
+  }
+}
+
+template <int D>
+__device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tmem, volatile int* abort,
+                             int item_begin, int item_end) {
+  using C = Cfg<D>;
+  const int i = threadIdx.x / 128;         // query tile of this warpgroup
+  const int wq = (threadIdx.x / 32) & 3;   // warp inside the warpgroup
+  const int lane = threadIdx.x & 31;
+  const int row = wq * 32 + lane;          // = TMEM lane
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+  const int32_t* items = p.plan + p.plan[H_OFF_ITEMS];
+  const float sl2 = p.scale_log2;
+  uint32_t scount = 0;
+  for (int it = item_begin; it < item_end; ++it) {
+    const int k = it - item_begin;
+    const int32_t* I = items + it * kItemInts;
+    const int t0 = I[I_T0], t1 = I[I_T1];
+    const int kv_start = I[I_KV_START], kv_end = I[I_KV_END];
+    const int slot = (i == 0) ? I[I_SLOT0] : I[I_SLOT1];
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int t = t0; t < t1; ++t) {
+      if (!warp_wait(&bars[C::B_SFULL + i], scount & 1, abort)) return;
+      ++scount;
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_wait(lane_base + s_col(i) + c * 32, s[c]);
+      const int pos0 = t * kTileKeys;
+      const bool edge = pos0 < kv_start || pos0 + kTileKeys > kv_end;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float v = __uint_as_float(s[c][e]);
+          if (edge) {
+            const int pos = pos0 + c * 32 + e;
+            if (pos < kv_start || pos >= kv_end) v = -INFINITY;
+            s[c][e] = __float_as_uint(v);
+          }
+          mx = fmaxf(mx, v);
+        }
+      }
+      const float m_tile = mx * sl2;
+      if (t == t0) {
+        m_run = m_tile;
+      } else if (m_tile > m_run + 8.f) {
+        const float f = fast_exp2(m_run - m_tile);
+        l_run *= f;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32_wait(lane_base + o_col(i) + c * 32, o);
+          uint32_t lo[16], hi[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            lo[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+            hi[e] = __float_as_uint(__uint_as_float(o[16 + e]) * f);
+          }
+          tmem_st16(lane_base + o_col(i) + c * 32, lo);
+          tmem_st16(lane_base + o_col(i) + c * 32 + 16, hi);
+        }
+        m_run = m_tile;
+      }
+      const float neg_m = -m_run;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
+          sum += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(lane_base + s_col(i) + c * 16, pk);
+      }
+      l_run += sum;
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars[C::B_PFULL + i]);
+    }
+    // ---- epilogue: normalised O and base-2 LSE into the partial slot ----
+    if (!warp_wait(&bars[C::B_OFINAL + i], k & 1, abort)) return;
+    tc_fence_after();
+    if (slot >= 0) {
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      float* dst = p.partial + static_cast<int64_t>(slot) * C::kSlotFloats +
+                   static_cast<int64_t>(row) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32_wait(lane_base + o_col(i) + c * 32, o);
+        float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          d4[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
+                              __uint_as_float(o[4 * e + 2]) * inv,
+                              __uint_as_float(o[4 * e + 3]) * inv);
+        }
+      }
+      const float lse = l_run > 0.f ? m_run + fast_log2(l_run) : -INFINITY;
+      p.partial[static_cast<int64_t>(slot) * C::kSlotFloats + kTileRows * D + row] = lse;
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bars[C::B_OFREE + i]);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    prefix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                            const __grid_constant__ CUtensorMap tm_k,
+                            const __grid_constant__ CUtensorMap tm_v, const PrefixParams p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSmemBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int off_cta = p.plan[H_OFF_CTA];
+  const int item_begin = p.plan[off_cta + blockIdx.x];
+  const int item_end = p.plan[off_cta + blockIdx.x + 1];
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[C::B_QFULL], 1);
+    mbar_init(&bars[C::B_QFREE], 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bars[C::B_KFULL + s], 1);
+      mbar_init(&bars[C::B_VFULL + s], 1);
+      mbar_init(&bars[C::B_KVEMPTY + s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[C::B_SFULL + i], 1);
+      mbar_init(&bars[C::B_PFULL + i], 4);
+      mbar_init(&bars[C::B_OFINAL + i], 1);
+      mbar_init(&bars[C::B_OFREE + i], 4);
+    }
+    *abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == kTmaWarp && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) producer<D>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) mma_issuer<D>(p, smem, bars, tmem, abort, item_begin, item_end);
+    __syncwarp();
+  } else {
+    softmax_role<D>(p, bars, tmem, abort, item_begin, item_end);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 1);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &qres) == cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+  });
+  return fn;
+}
+
+int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box, const char* what) {
+  auto fn = get_encode_fn();
+  if (!fn) return fail(D2SD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  uint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult res = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
+                    strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) {
+    return fail(D2SD_ERR_INVALID_ARGUMENT,
+                std::string("cuTensorMapEncodeTiled failed for ") + what + " (CUresult " +
+                    std::to_string(static_cast<int>(res)) + ")");
+  }
+  return D2SD_OK;
+}
+
+template <int D>
+int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+           const PrefixParams& prm, int num_ctas, cudaStream_t stream) {
+  using C = Cfg<D>;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(prefix_attention_kernel<D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (e != cudaSuccess)
+      return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured_device = dev;
+  }
+  prefix_attention_kernel<D><<<num_ctas, kNumThreads, C::kSmemBytes, stream>>>(tq, tk, tv, prm);
+  return check_launch("prefix_attention_kernel");
+}
+
+}  // namespace
+}  // namespace d2sd
+
+extern "C" int64_t d2sd_partial_slot_bytes(int32_t head_dim) {
+  return static_cast<int64_t>(d2sd::plan::kTileRows) * (head_dim + 1) * 4;
+}
+
+extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                     int64_t num_q_tokens, const void* k, const void* v,
+                                     int64_t kv_stride_page, int64_t kv_stride_slot,
+                                     int64_t kv_stride_head, int32_t page_size, int64_t num_pages,
+                                     const int32_t* page_table, const int32_t* page_table_offset,
+                                     int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+                                     float sm_scale, const int32_t* plan, int32_t num_ctas,
+                                     void* partial, int64_t partial_bytes, int32_t* status,
+                                     void* stream) {
+  using namespace d2sd;
+  if (!q || !k || !v || !plan || !partial || num_q_tokens <= 0 || num_pages <= 0 ||
+      num_qo_heads <= 0 || num_kv_heads <= 0 || num_qo_heads % num_kv_heads != 0)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_prefix_attention: invalid argument");
+  if (num_ctas <= 0) return D2SD_OK;  // empty plan: nothing to attend
+  if (head_dim != 64 && head_dim != 128)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_prefix_attention: head_dim must be 64 or 128");
+  const int G = num_qo_heads / num_kv_heads;
+  if (plan::kTileRows % G != 0)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_prefix_attention: qo heads per kv head must divide 128");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(partial) ||
+      q_stride_token % 8 || q_stride_head % 8 || kv_stride_slot % 8 || kv_stride_head % 8 ||
+      (page_table && kv_stride_page % 8))
+    return fail(D2SD_ERR_INVALID_ARGUMENT,
+                "d2sd_prefix_attention: pointers must be 16-byte aligned and strides multiples of 8");
+  if (page_table && (page_size % 8 != 0 || page_size <= 0 || plan::kTileKeys % page_size != 0))
+    return fail(D2SD_ERR_UNSUPPORTED,
+                "d2sd_prefix_attention: page_size must be a multiple of 8 dividing 128");
+  if (page_table && !page_table_offset)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_prefix_attention: page_table_offset is required");
+  if (partial_bytes <= 0)
+    return fail(D2SD_ERR_WORKSPACE, "d2sd_prefix_attention: empty partial workspace");
+
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(num_qo_heads),
+                              static_cast<uint64_t>(num_q_tokens)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(q_stride_head) * 2,
+                                 static_cast<uint64_t>(q_stride_token) * 2};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(G), static_cast<uint32_t>(plan::kTileRows / G)};
+    int rc = encode_bf16_map(&tq, q, 3, dims, strides, box, "q");
+    if (rc) return rc;
+  }
+  int rows_per_box;
+  {
+    uint64_t dims[4], strides[3];
+    uint32_t box[4];
+    if (page_table) {
+      rows_per_box = page_size;
+      dims[0] = head_dim;
+      dims[1] = page_size;
+      dims[2] = num_kv_heads;
+      dims[3] = num_pages;
+      strides[0] = kv_stride_slot * 2;
+      strides[1] = kv_stride_head * 2;
+      strides[2] = kv_stride_page * 2;
+    } else {
+      rows_per_box = 16;
+      dims[0] = head_dim;
+      dims[1] = num_pages;  // tokens
+      dims[2] = num_kv_heads;
+      dims[3] = 1;
+      strides[0] = kv_stride_slot * 2;
+      strides[1] = kv_stride_head * 2;
+      strides[2] = static_cast<uint64_t>(kv_stride_slot) * 2 * static_cast<uint64_t>(num_pages);
+      if (strides[2] < strides[1]) strides[2] = strides[1] * num_kv_heads;
+    }
+    box[0] = 64;
+    box[1] = static_cast<uint32_t>(rows_per_box);
+    box[2] = 1;
+    box[3] = 1;
+    int rc = encode_bf16_map(&tk, k, 4, dims, strides, box, "k");
+    if (rc) return rc;
+    rc = encode_bf16_map(&tv, v, 4, dims, strides, box, "v");
+    if (rc) return rc;
+  }
+  PrefixParams prm;
+  prm.plan = plan;
+  prm.page_table = page_table;
+  prm.page_table_offset = page_table_offset;
+  prm.partial = static_cast<float*>(partial);
+  prm.status = status;
+  prm.rows_per_box = rows_per_box;
+  prm.G = G;
+  prm.scale_log2 = sm_scale * kLog2e;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 128) return launch<128>(tq, tk, tv, prm, num_ctas, st);
+  return launch<64>(tq, tk, tv, prm, num_ctas, st);
+}

@@ -1,0 +1,117 @@
+"""Paged target KV cache and the accepted-branch commit (kernel (d)).
+
+The reference keeps the target cache in a transformers DynamicCache and, after
+every verify step, rebuilds every layer with torch.cat([layer.keys,
+new_K[vb, :, :acc]], dim=2) (generation/d3_generator.py:227-232) -- a full
+reallocation and copy of the cache, O(L * P) bytes per step. ``PagedKVCache``
+holds fixed-capacity page pools instead; ``commit`` moves only the acc accepted
+rows of every layer in one launch, reading acc and the winning branch from the
+acceptance kernel's device result.
+
+Pool layout per layer: [num_pages, Hk, page_size, D] ("HND" pages: one
+contiguous 16 x D block per (page, head), the unit kernel (a) fetches with one
+TMA box). Pools are zero-initialised so every slot past a sequence's length
+holds finite values.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import ops
+
+
+class PagedKVCache:
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_tokens: int,
+                 page_size: int = 16, dtype: torch.dtype = torch.bfloat16, device="cuda",
+                 page_order: torch.Tensor | None = None):
+        self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
+        self.page_size = page_size
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.num_pages = -(-max_tokens // page_size)
+        shape = (num_layers, self.num_pages, num_kv_heads, page_size, head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=self.device)
+        self.v = torch.zeros(shape, dtype=dtype, device=self.device)
+        # logical page i of the sequence -> physical page page_table[i]
+        if page_order is None:
+            page_order = torch.arange(self.num_pages)
+        if page_order.numel() != self.num_pages:
+            raise ValueError("page_order must list every page once")
+        self.page_table = page_order.to(torch.int32).to(self.device)
+        self.length = 0
+        self._ptr_cache: dict = {}
+
+    # -- views -------------------------------------------------------------
+    def layer(self, l: int):
+        """(k_pool, v_pool) of layer l, [num_pages, Hk, page_size, D]."""
+        return self.k[l], self.v[l]
+
+    kv_layout = "paged_hnd"
+
+    def positions_to_slots(self, pos: torch.Tensor):
+        pt = self.page_table.to(pos.device).long()
+        return pt[pos // self.page_size], pos % self.page_size
+
+    # -- host-side set-up (not on the hot path) ------------------------------
+    def write(self, l: int, k: torch.Tensor, v: torch.Tensor, start: int = 0) -> None:
+        """Write k, v [n, Hk, D] at positions start .. start+n-1 of layer l."""
+        n = k.shape[0]
+        pos = torch.arange(start, start + n, device=self.device)
+        page, slot = self.positions_to_slots(pos)
+        self.k[l, page, :, slot] = k.to(self.dtype)
+        self.v[l, page, :, slot] = v.to(self.dtype)
+
+    def gather(self, l: int, length: int | None = None):
+        """Layer l as contiguous [length, Hk, D] tensors (for checks)."""
+        n = self.length if length is None else length
+        pos = torch.arange(n, device=self.device)
+        page, slot = self.positions_to_slots(pos)
+        return self.k[l, page, :, slot], self.v[l, page, :, slot]
+
+    # -- kernel (d) ------------------------------------------------------------
+    def _layer_ptrs(self, new_k, new_v):
+        key = (tuple(t.data_ptr() for t in new_k), tuple(t.data_ptr() for t in new_v))
+        ptrs = self._ptr_cache.get(key)
+        if ptrs is None:
+            vals = []
+            for l in range(self.num_layers):
+                vals += [new_k[l].data_ptr(), new_v[l].data_ptr(), self.k[l].data_ptr(),
+                         self.v[l].data_ptr()]
+            ptrs = torch.tensor(vals, dtype=torch.int64).to(self.device)
+            if len(self._ptr_cache) > 16:
+                self._ptr_cache.clear()
+            self._ptr_cache[key] = ptrs
+        return ptrs
+
+    def commit(self, new_k, new_v, accept_result: torch.Tensor, advance_by: int | None = None,
+               cache_len: int | None = None) -> None:
+        """Append block positions 0..acc-1 of the winning branch to every layer.
+
+        new_k/new_v: per-layer [B, Hk, T, D] tensors (a list, or a stacked
+        [L, B, Hk, T, D] tensor) with identical strides; accept_result: the
+        device int32 {acc, branch} of kernel (c). The rows land at positions
+        cache_len (default: self.length) onward. ``advance_by`` (the host copy
+        of acc, when the caller has read it) moves self.length forward.
+        """
+        if isinstance(new_k, torch.Tensor):
+            new_k = [new_k[l] for l in range(new_k.shape[0])]
+            new_v = [new_v[l] for l in range(new_v.shape[0])]
+        if len(new_k) != self.num_layers or len(new_v) != self.num_layers:
+            raise ValueError("one new K/V tensor per layer is required")
+        s = new_k[0].stride()
+        for t in list(new_k) + list(new_v):
+            if t.stride() != s or t.dtype != self.dtype or t.stride(-1) != 1:
+                raise ValueError("new K/V tensors must share strides and the cache dtype")
+        B, Hk, T, D = new_k[0].shape
+        start = self.length if cache_len is None else cache_len
+        if start + T > self.num_pages * self.page_size:
+            raise ValueError("cache capacity exceeded")
+        kl = self.k[0]
+        ops.commit_kv(self._layer_ptrs(new_k, new_v), num_layers=self.num_layers,
+                      num_kv_heads=Hk, head_dim=D, elem_bytes=self.k.element_size(), block_len=T,
+                      new_strides=(s[0], s[1], s[2]),
+                      cache_strides=(kl.stride(0), kl.stride(2), kl.stride(1)),
+                      page_size=self.page_size, page_table=self.page_table,
+                      accept_result=accept_result, cache_len=start)
+        if advance_by is not None:
+            self.length = start + int(advance_by)

@@ -1,0 +1,262 @@
+"""torch-tensor front end of the C ABI: argument checks, strides, streams.
+
+Each function maps tensors onto one ``d2sd_*`` entry point of ``libd2sd.so`` and
+launches on the current CUDA stream. Nothing here computes on the host; if the
+library is missing the import of ``d2sd_b200._lib.load`` raises.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, load
+
+_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16,
+           torch.float16: _lib.DTYPE_F16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}") from None
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("d2sd kernels take CUDA tensors (there is no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("all tensors must be on the same device")
+    return dev
+
+
+def num_sms(device: torch.device | None = None) -> int:
+    return torch.cuda.get_device_properties(device or torch.cuda.current_device()).multi_processor_count
+
+
+# ---------------------------------------------------------------------------
+# KV views
+# ---------------------------------------------------------------------------
+@dataclass
+class KVView:
+    """How kernel (a) addresses a K or V tensor.
+
+    layout "paged_hnd": [pages, Hk, page_size, D]; "paged_nhd": [pages,
+    page_size, Hk, D]; "nhd": [tokens, Hk, D] (FlashInfer's NHD, the layout of
+    generation/verification.py:139-140 after its transpose copy); "hnd":
+    [Hk, tokens, D] (a DynamicCache layer [1, Hk, P, D] with the batch index
+    dropped -- read in place, no transpose copy).
+    """
+    stride_page: int
+    stride_slot: int
+    stride_head: int
+    page_size: int
+    num_pages: int  # pages (paged) or tokens (contiguous)
+    num_kv_heads: int
+    head_dim: int
+    paged: bool
+
+
+def kv_view(t: torch.Tensor, layout: str) -> KVView:
+    if t.stride(-1) != 1:
+        raise ValueError("the head dimension of K/V must be contiguous")
+    if layout == "paged_hnd":
+        P, H, S, D = t.shape
+        return KVView(t.stride(0), t.stride(2), t.stride(1), S, P, H, D, True)
+    if layout == "paged_nhd":
+        P, S, H, D = t.shape
+        return KVView(t.stride(0), t.stride(1), t.stride(2), S, P, H, D, True)
+    if layout == "nhd":
+        N, H, D = t.shape
+        return KVView(0, t.stride(0), t.stride(1), 16, N, H, D, False)
+    if layout == "hnd":
+        H, N, D = t.shape
+        return KVView(0, t.stride(1), t.stride(0), 16, N, H, D, False)
+    raise ValueError(f"unknown kv layout {layout!r}")
+
+
+# ---------------------------------------------------------------------------
+# (a) shared-prefix attention
+# ---------------------------------------------------------------------------
+def prefix_plan(q_tokens, q_token_offset, kv_start, kv_end, num_qo_heads: int,
+                num_kv_heads: int, num_ctas: int):
+    """Host-side work plan (d2sd_prefix_plan). Returns (plan int32 numpy array,
+    number of partial slots)."""
+    lib = load()
+    arrs = [np.ascontiguousarray(np.asarray(a, dtype=np.int32)) for a in
+            (q_tokens, q_token_offset, kv_start, kv_end)]
+    R = len(arrs[0])
+    if any(len(a) != R for a in arrs):
+        raise ValueError("per-request arrays must have equal length")
+    total = int(max((int(o) + int(n) for o, n in zip(arrs[1], arrs[0])), default=0))
+    cap = lib.d2sd_prefix_plan_capacity(R, num_qo_heads, num_kv_heads, num_ctas, total)
+    if cap < 0:
+        raise ValueError("invalid plan sizes")
+    plan = np.zeros(cap, dtype=np.int32)
+    nslots = np.zeros(1, dtype=np.int32)
+    rc = lib.d2sd_prefix_plan(*(a.ctypes.data for a in arrs), R, num_qo_heads, num_kv_heads,
+                              num_ctas, plan.ctypes.data, cap, nslots.ctypes.data)
+    check(rc, "d2sd_prefix_plan")
+    used = int(plan[11]) + int(plan[6])  # H_OFF_TOKENS + H_NUM_TOKENS
+    return plan[:used].copy(), int(nslots[0])
+
+
+def partial_slot_bytes(head_dim: int) -> int:
+    return int(load().d2sd_partial_slot_bytes(head_dim))
+
+
+def prefix_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_layout: str,
+                     plan_dev: torch.Tensor, num_ctas: int, partial: torch.Tensor,
+                     sm_scale: float, page_table: torch.Tensor | None = None,
+                     page_table_offset: torch.Tensor | None = None,
+                     status: torch.Tensor | None = None) -> None:
+    """Launch kernel (a). q [tokens, Hq, D] bf16; k/v per ``kv_layout``."""
+    dev = _require_cuda(q, k, v, plan_dev, partial, page_table, page_table_offset, status)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError("prefix attention takes bf16 q/k/v")
+    if q.dim() != 3 or q.stride(-1) != 1:
+        raise ValueError("q must be [tokens, heads, head_dim] with a contiguous head_dim")
+    kvw = kv_view(k, kv_layout)
+    vvw = kv_view(v, kv_layout)
+    if (kvw.stride_page, kvw.stride_slot, kvw.stride_head) != (vvw.stride_page, vvw.stride_slot,
+                                                                 vvw.stride_head):
+        raise ValueError("k and v must share a layout")
+    if kvw.paged != (page_table is not None):
+        raise ValueError("paged layouts need a page table, contiguous ones must not have one")
+    N, Hq, D = q.shape
+    if D != kvw.head_dim:
+        raise ValueError("q and k head_dim differ")
+    rc = load().d2sd_prefix_attention(
+        q.data_ptr(), q.stride(0), q.stride(1), N, k.data_ptr(), v.data_ptr(), kvw.stride_page,
+        kvw.stride_slot, kvw.stride_head, kvw.page_size, kvw.num_pages, _ptr(page_table),
+        _ptr(page_table_offset), Hq, kvw.num_kv_heads, D, float(sm_scale), plan_dev.data_ptr(),
+        int(num_ctas), partial.data_ptr(), partial.numel() * partial.element_size(),
+        _ptr(status), _stream(dev))
+    check(rc, "d2sd_prefix_attention")
+
+
+# ---------------------------------------------------------------------------
+# (b) suffix attention + merge
+# ---------------------------------------------------------------------------
+def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
+                 v_local: torch.Tensor | None, out: torch.Tensor, lse: torch.Tensor | None,
+                 *, num_blocks: int, block_len: int, num_qo_heads: int, num_kv_heads: int,
+                 sm_scale: float, mask_mode: int = _lib.MASK_CAUSAL,
+                 custom_mask: torch.Tensor | None = None, partial: torch.Tensor | None = None,
+                 plan_dev: torch.Tensor | None = None, prefix_token: torch.Tensor | None = None,
+                 prefix_out: torch.Tensor | None = None, prefix_lse: torch.Tensor | None = None,
+                 sinks: torch.Tensor | None = None, sink_mode: int = _lib.SINK_NONE) -> None:
+    """Launch kernel (b). Token-major 3-D views: q/out [tokens, Hq, D],
+    k/v_local [tokens, Hk, D], lse/prefix_lse [tokens, Hq]."""
+    dev = _require_cuda(q, k_local, v_local, out, lse, custom_mask, partial, plan_dev,
+                        prefix_token, prefix_out, prefix_lse, sinks)
+    for t in (q, k_local, v_local, out, prefix_out):
+        if t is not None and (t.dim() != 3 or t.stride(-1) != 1):
+            raise ValueError("token tensors must be [tokens, heads, head_dim], head_dim contiguous")
+    for t in (lse, prefix_lse):
+        if t is not None and (t.dtype != torch.float32 or t.stride(-1) != 1):
+            raise ValueError("lse tensors must be fp32 with a contiguous head axis")
+    if k_local is not None and (k_local.stride() != v_local.stride()):
+        raise ValueError("k_local and v_local must share strides")
+    if sinks is not None and (sinks.dtype != torch.float32 or not sinks.is_contiguous()):
+        raise ValueError("sinks must be a contiguous fp32 tensor")
+    D = out.shape[-1]
+    kst = k_local.stride(0) if k_local is not None else 0
+    ksh = k_local.stride(1) if k_local is not None else 0
+    rc = load().d2sd_suffix_merge(
+        _ptr(q), q.stride(0) if q is not None else 0, q.stride(1) if q is not None else 0,
+        _ptr(k_local), _ptr(v_local), kst, ksh, int(num_blocks), int(block_len), int(mask_mode),
+        _ptr(custom_mask), _ptr(partial), _ptr(plan_dev), _ptr(prefix_token), _ptr(prefix_out),
+        prefix_out.stride(0) if prefix_out is not None else 0,
+        prefix_out.stride(1) if prefix_out is not None else 0, _ptr(prefix_lse),
+        prefix_lse.stride(0) if prefix_lse is not None else 0, out.data_ptr(), out.stride(0),
+        out.stride(1), _ptr(lse), lse.stride(0) if lse is not None else 0, _ptr(sinks),
+        int(sink_mode), int(num_qo_heads), int(num_kv_heads), int(D), dtype_code(out),
+        float(sm_scale), _stream(dev))
+    check(rc, "d2sd_suffix_merge")
+
+
+def merge_state(v: torch.Tensor, s: torch.Tensor, v_other: torch.Tensor,
+                s_other: torch.Tensor) -> None:
+    """In-place (v, s) <- merge((v, s), (v_other, s_other)); v [n, H, D], s [n, H]."""
+    dev = _require_cuda(v, s, v_other, s_other)
+    if v.dim() != 3 or v.shape != v_other.shape or s.shape != v.shape[:2] or s_other.shape != s.shape:
+        raise ValueError("merge_state: v [n, H, D], s [n, H] with matching shapes")
+    if v.stride(-1) != 1 or v_other.stride(-1) != 1 or s.stride(-1) != 1 or s_other.stride(-1) != 1:
+        raise ValueError("merge_state: innermost dims must be contiguous")
+    if s.dtype != torch.float32 or s_other.dtype != torch.float32 or v.dtype != v_other.dtype:
+        raise ValueError("merge_state: fp32 lse and matching value dtypes")
+    n, H, D = v.shape
+    rc = load().d2sd_merge_state(v.data_ptr(), v.stride(0), v.stride(1), s.data_ptr(), s.stride(0),
+                                 v_other.data_ptr(), v_other.stride(0), v_other.stride(1),
+                                 s_other.data_ptr(), s_other.stride(0), n, H, D, dtype_code(v),
+                                 _stream(dev))
+    check(rc, "d2sd_merge_state")
+
+
+# ---------------------------------------------------------------------------
+# (c) acceptance
+# ---------------------------------------------------------------------------
+def accept_workspace_bytes(num_branches: int, block_len: int, vocab: int) -> int:
+    return int(load().d2sd_verify_accept_workspace_size(num_branches, block_len, vocab))
+
+
+def verify_accept(logits: torch.Tensor, block_ids: torch.Tensor, result: torch.Tensor,
+                  accepted_ids: torch.Tensor, workspace: torch.Tensor,
+                  argmax_out: torch.Tensor | None = None) -> None:
+    """Launch kernel (c). logits [B, T, V] (vocab contiguous), block_ids int64 [B, T],
+    result int32 [2], accepted_ids int64 [T], workspace zero-initialised bytes."""
+    dev = _require_cuda(logits, block_ids, result, accepted_ids, workspace, argmax_out)
+    if logits.dim() != 3 or logits.stride(-1) != 1:
+        raise ValueError("logits must be [branches, block, vocab] with a contiguous vocab axis")
+    B, T, V = logits.shape
+    if block_ids.shape != (B, T) or block_ids.dtype != torch.int64:
+        raise ValueError("block_ids must be int64 [branches, block]")
+    if result.dtype != torch.int32 or result.numel() < 2:
+        raise ValueError("result must be int32 with 2 entries")
+    if accepted_ids.dtype != torch.int64 or accepted_ids.numel() < T:
+        raise ValueError("accepted_ids must be int64 with block entries")
+    rc = load().d2sd_verify_accept(
+        logits.data_ptr(), dtype_code(logits), B, T, V, logits.stride(0), logits.stride(1),
+        block_ids.data_ptr(), block_ids.stride(0), block_ids.stride(1), result.data_ptr(),
+        accepted_ids.data_ptr(), _ptr(argmax_out), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _stream(dev))
+    check(rc, "d2sd_verify_accept")
+
+
+# ---------------------------------------------------------------------------
+# (d) KV commit
+# ---------------------------------------------------------------------------
+def commit_kv(layer_ptrs: torch.Tensor, *, num_layers: int, num_kv_heads: int, head_dim: int,
+              elem_bytes: int, block_len: int, new_strides: tuple[int, int, int],
+              cache_strides: tuple[int, int, int], page_size: int,
+              page_table: torch.Tensor | None, accept_result: torch.Tensor,
+              cache_len_dev: torch.Tensor | None = None, cache_len: int = 0) -> None:
+    """Launch kernel (d). layer_ptrs: int64 device tensor [L*4] of
+    {new_k, new_v, cache_k, cache_v} pointers; strides in elements:
+    new (branch, head, token), cache (page, slot, head)."""
+    dev = _require_cuda(layer_ptrs, page_table, accept_result, cache_len_dev)
+    rc = load().d2sd_commit_kv(layer_ptrs.data_ptr(), num_layers, num_kv_heads, head_dim,
+                               elem_bytes, block_len, *new_strides, *cache_strides, page_size,
+                               _ptr(page_table), accept_result.data_ptr(), _ptr(cache_len_dev),
+                               int(cache_len), _stream(dev))
+    check(rc, "d2sd_commit_kv")

@@ -1,0 +1,232 @@
+/*
+ * d2sd.h - C ABI of the B200 (sm_100a) tree-verification hot path of D2-SD.
+ *
+ * Every entry point takes plain device pointers, element strides, sizes and a
+ * cudaStream_t (passed as void*), returns an int status (D2SD_OK == 0) and
+ * never allocates device memory, never synchronises the host and never frees
+ * anything: workspaces are passed in by the caller. All work is enqueued on the
+ * caller's stream, so every launch is capturable in a CUDA graph.
+ *
+ * Reference call sites each entry point replaces (paths inside catnanami/D2-SD):
+ *   d2sd_prefix_plan / d2sd_prefix_attention
+ *       flashinfer.single_prefill_with_kv_cache(q_all, k_shared, v_shared,
+ *       causal=False, return_lse=True)  generation/verification.py:145-148,
+ *       model/dflash.py:112-115 (level 1 of the cascade).
+ *   d2sd_suffix_merge
+ *       CascadeGraphRunner.run (model/cascade_graph.py:76-112, the graph body at
+ *       :52-60: per-branch single_prefill + merge_state_in_place), the loop at
+ *       generation/verification.py:158-165 and the GPT-OSS sink rescale at
+ *       generation/verification.py:173-176.
+ *   d2sd_merge_state
+ *       flashinfer.merge_state_in_place(v, s, v_other, s_other)
+ *       model/cascade_graph.py:58-60, generation/verification.py:163-165.
+ *   d2sd_verify_accept
+ *       the greedy acceptance walk generation/d3_generator.py:204-225 with
+ *       model/utils.py:28-32 (sample, temperature 0), and its single-branch
+ *       form generation/dflash_generator.py:110-125.
+ *   d2sd_commit_kv
+ *       the accepted-branch KV append generation/d3_generator.py:227-232.
+ */
+#ifndef D2SD_H_
+#define D2SD_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define D2SD_OK 0
+#define D2SD_ERR_INVALID_ARGUMENT 1  /* shape, stride, dtype or pointer rejected */
+#define D2SD_ERR_UNSUPPORTED 2       /* valid request outside the built kernels */
+#define D2SD_ERR_WORKSPACE 3         /* workspace / plan buffer too small */
+#define D2SD_ERR_CUDA 4              /* a CUDA runtime/driver call failed */
+#define D2SD_ERR_NO_DEVICE 5         /* no sm_100 device current */
+
+/* ---- dtypes ------------------------------------------------------------ */
+#define D2SD_DTYPE_F32 0
+#define D2SD_DTYPE_BF16 1
+#define D2SD_DTYPE_F16 2
+
+/* ---- suffix mask modes (d2sd_suffix_merge) ----------------------------- */
+#define D2SD_MASK_NONE 0    /* every block token sees the whole block (DTA) */
+#define D2SD_MASK_CAUSAL 1  /* token t sees tokens 0..t of its block (verify) */
+#define D2SD_MASK_CUSTOM 2  /* token t sees the set bits of mask[block][t] */
+
+/* ---- sink modes (d2sd_suffix_merge) ------------------------------------ */
+#define D2SD_SINK_NONE 0
+/* out *= sigmoid(lse2 - sink): the formula of generation/verification.py:173-176,
+ * where lse2 is the base-2 log-sum-exp and sink is a natural-log logit. */
+#define D2SD_SINK_REFERENCE 1
+/* out *= sigmoid(lse2 * ln2 - sink): the softmax-with-sink of the HF GPT-OSS
+ * attention (an extra exp(sink) term in the denominator). */
+#define D2SD_SINK_EXACT 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+int d2sd_version(void);
+
+/* Human-readable text of the last error raised on the calling host thread. */
+const char* d2sd_last_error(void);
+
+/* Number of int32 entries a prefix plan needs (upper bound). */
+int64_t d2sd_prefix_plan_capacity(int32_t num_requests, int32_t num_qo_heads,
+                                  int32_t num_kv_heads, int32_t num_ctas,
+                                  int64_t total_q_tokens);
+
+/* Host-side work partition of the shared-prefix attention.
+ *
+ * Request r has q_tokens[r] query tokens (rows q_token_offset[r] ..
+ * q_token_offset[r]+q_tokens[r]-1 of the Q tensor) and attends the prefix keys
+ * kv_start[r] .. kv_end[r]-1 (absolute positions inside its KV sequence; the
+ * sliding-window truncation of generation/verification.py:130-135 is
+ * kv_start = kv_end - window). num_ctas is the persistent grid (the SM count).
+ * The plan is written into plan[0 .. capacity) on the HOST; copy it to device
+ * memory before d2sd_prefix_attention. *num_partial_slots receives the number of
+ * 128-row partial-state slots the launch writes (workspace sizing).
+ * Pure host code: callable without a GPU. */
+int d2sd_prefix_plan(const int32_t* q_tokens, const int32_t* q_token_offset,
+                     const int32_t* kv_start, const int32_t* kv_end,
+                     int32_t num_requests, int32_t num_qo_heads,
+                     int32_t num_kv_heads, int32_t num_ctas, int32_t* plan,
+                     int64_t capacity, int32_t* num_partial_slots);
+
+/* Bytes of partial state per slot: 128 rows x (head_dim + 1) fp32. */
+int64_t d2sd_partial_slot_bytes(int32_t head_dim);
+
+/* Shared-prefix (level-1) attention on tcgen05/TMEM.
+ *
+ * q:        bf16 [tokens, num_qo_heads, head_dim], strides in elements
+ *           (q_stride_token, q_stride_head), dim stride 1.
+ * k, v:     bf16 KV of the prefix. Paged (page_table != NULL): element
+ *           (page, slot, head, d) at page*kv_stride_page + slot*kv_stride_slot
+ *           + head*kv_stride_head + d, page_size slots per page, num_pages pages;
+ *           request r's position p lives in page
+ *           page_table[page_table_offset[r] + p / page_size].
+ *           Contiguous (page_table == NULL): element (token, head, d) at
+ *           token*kv_stride_slot + head*kv_stride_head + d with num_pages
+ *           tokens in total, and request r's position p is token
+ *           page_table_offset[r] + p.
+ * plan:     device copy of d2sd_prefix_plan's output.
+ * partial:  device workspace of num_partial_slots * d2sd_partial_slot_bytes.
+ * Writes, for every query row, the normalised prefix output and its base-2
+ * log-sum-exp (the FlashInfer convention) into the partial slots; the rows are
+ * combined by d2sd_suffix_merge. head_dim is 64 or 128; the group size
+ * num_qo_heads / num_kv_heads divides 128; page_size is a multiple of 8 that
+ * divides 128. Pool slots past a request's last position must hold finite
+ * values (the pools this library allocates are zero-initialised).
+ * status (device int32, may be NULL) receives a nonzero code if a pipeline
+ * wait inside the kernel ran out of time; the kernel then returns early. */
+int d2sd_prefix_attention(const void* q, int64_t q_stride_token,
+                          int64_t q_stride_head, int64_t num_q_tokens,
+                          const void* k, const void* v, int64_t kv_stride_page,
+                          int64_t kv_stride_slot, int64_t kv_stride_head,
+                          int32_t page_size, int64_t num_pages,
+                          const int32_t* page_table,
+                          const int32_t* page_table_offset,
+                          int32_t num_qo_heads, int32_t num_kv_heads,
+                          int32_t head_dim, float sm_scale,
+                          const int32_t* plan, int32_t num_ctas,
+                          void* partial, int64_t partial_bytes,
+                          int32_t* status, void* stream);
+
+/* Level-2 (per-block suffix) attention fused with the log-sum-exp merge of
+ * both levels and, optionally, the attention-sink rescale.
+ *
+ * Tokens are grouped in blocks of block_len consecutive tokens (one block per
+ * draft branch). q, k_local, v_local: [num_blocks*block_len, heads, head_dim]
+ * with (token, head) element strides; k_local/v_local may be NULL for a pure
+ * merge (no level 2).
+ * Prefix state, one of:
+ *   - partial != NULL: merged from the slots written by d2sd_prefix_attention;
+ *     prefix_token[t] (device, may be NULL = identity) maps block token t to
+ *     its row in the prefix-attention Q tensor; plan is the device plan.
+ *   - partial == NULL, prefix_out != NULL: a dense state (out [tokens, Hq, D]
+ *     in the q dtype, lse [tokens, Hq] fp32 base-2) as produced by
+ *     single_prefill_with_kv_cache; the CascadeGraphRunner.run in-place form.
+ *   - neither: no prefix (level 2 alone).
+ * out/lse receive the merged output (q dtype) and base-2 LSE; they may alias
+ * prefix_out/prefix_lse. mask_mode is a D2SD_MASK_*, custom_mask is
+ * uint64 [num_blocks*block_len] (bit j = token may see block token j).
+ * sinks: fp32 [num_qo_heads] or NULL; sink_mode a D2SD_SINK_*. */
+int d2sd_suffix_merge(const void* q, int64_t q_stride_token,
+                      int64_t q_stride_head, const void* k_local,
+                      const void* v_local, int64_t kv_stride_token,
+                      int64_t kv_stride_head, int32_t num_blocks,
+                      int32_t block_len, int32_t mask_mode,
+                      const uint64_t* custom_mask, const void* partial,
+                      const int32_t* plan, const int32_t* prefix_token,
+                      const void* prefix_out, int64_t prefix_out_stride_token,
+                      int64_t prefix_out_stride_head, const float* prefix_lse,
+                      int64_t prefix_lse_stride_token, void* out,
+                      int64_t out_stride_token, int64_t out_stride_head,
+                      float* lse, int64_t lse_stride_token,
+                      const float* sinks, int32_t sink_mode,
+                      int32_t num_qo_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t dtype, float sm_scale,
+                      void* stream);
+
+/* In-place merge of two attention states (v,s) <- merge((v,s),(v_other,s_other))
+ * with base-2 LSEs: v [n, heads, head_dim] (dtype), s [n, heads] fp32. */
+int d2sd_merge_state(void* v, int64_t v_stride_token, int64_t v_stride_head,
+                     float* s, int64_t s_stride_token, const void* v_other,
+                     int64_t vo_stride_token, int64_t vo_stride_head,
+                     const float* s_other, int64_t so_stride_token, int64_t n,
+                     int32_t heads, int32_t head_dim, int32_t dtype,
+                     void* stream);
+
+/* Workspace bytes for d2sd_verify_accept; must be zeroed once before its
+ * first use (the kernel leaves it zeroed again on exit). */
+int64_t d2sd_verify_accept_workspace_size(int32_t num_branches,
+                                          int32_t block_len, int64_t vocab);
+
+/* Greedy multi-branch acceptance over target logits in one launch, no host
+ * synchronisation.
+ * logits: [num_branches, block_len, vocab] (dtype F32/BF16/F16), strides in
+ *         elements (branch, pos), vocab stride 1.
+ * block_ids: int64 [num_branches, block_len] (branch, pos strides); column 0
+ *         is the anchor token.
+ * result (device int32[2]): result[0] = acceptance_length in [1, block_len]
+ *         (includes the bonus token), result[1] = the winning branch.
+ * accepted_ids (device int64[block_len]): the accepted tokens, bonus last;
+ *         entries at and after acceptance_length are set to -1.
+ * argmax_out (device int64[num_branches*block_len] or NULL): the per-position
+ *         argmax of every branch (first maximal index, NaN counts as maximal).
+ * num_branches <= 64. */
+int d2sd_verify_accept(const void* logits, int32_t dtype,
+                       int32_t num_branches, int32_t block_len, int64_t vocab,
+                       int64_t stride_branch, int64_t stride_pos,
+                       const int64_t* block_ids, int64_t ids_stride_branch,
+                       int64_t ids_stride_pos, int32_t* result,
+                       int64_t* accepted_ids, int64_t* argmax_out,
+                       void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Accepted-branch KV commit for all layers in one launch.
+ * layer_ptrs: device array of num_layers*4 pointers
+ *   {new_k, new_v, cache_k, cache_v} per layer.
+ * new_k/new_v: [num_branches, heads, block_len, head_dim] with element strides
+ *   (new_stride_branch, new_stride_head, new_stride_token), dim stride 1.
+ * cache: position p of head h at
+ *   page_table[p / page_size]*cache_stride_page + (p % page_size)*cache_stride_slot
+ *   + h*cache_stride_head (page_table == NULL: page index p / page_size).
+ * accept_result: the device int32[2] {acceptance_length, branch} written by
+ *   d2sd_verify_accept; block positions 0..acceptance_length-1 of the winning
+ *   branch are written to cache positions cache_len .. cache_len+acc-1, where
+ *   cache_len = *cache_len_dev if cache_len_dev != NULL else cache_len_host.
+ * elem_bytes is 2 or 4; head_dim*elem_bytes a multiple of 16. */
+int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
+                   int32_t num_kv_heads, int32_t head_dim, int32_t elem_bytes,
+                   int32_t block_len, int64_t new_stride_branch,
+                   int64_t new_stride_head, int64_t new_stride_token,
+                   int64_t cache_stride_page, int64_t cache_stride_slot,
+                   int64_t cache_stride_head, int32_t page_size,
+                   const int32_t* page_table, const int32_t* accept_result,
+                   const int32_t* cache_len_dev, int64_t cache_len_host,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* D2SD_H_ */

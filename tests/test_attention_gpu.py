@@ -1,0 +1,250 @@
+"""Kernels (a) and (b) against the CPU oracle on identical seeded inputs.
+
+Tolerance (north star): bf16 attention outputs within 2e-2 absolute / 1e-2
+relative of the float64 oracle; base-2 LSEs within 1e-2 absolute.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_cases
+from oracle import attention as AT
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL, LSE_ATOL = 2e-2, 1e-2, 1e-2
+
+
+def f64(t):
+    return t.detach().double().cpu().numpy()
+
+
+def rand(shape, gen, dev, scale=1.0):
+    return (torch.randn(shape, generator=gen) * scale).to(torch.bfloat16).to(dev)
+
+
+def close(a, b, atol=ATOL, rtol=RTOL):
+    np.testing.assert_allclose(f64(a) if torch.is_tensor(a) else a, b, atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("N,P,Hq,Hk,D", [
+    (64, 512, 32, 8, 128),     # BASELINE config-1 shapes
+    (64, 300, 32, 8, 128),     # prefix not a multiple of the 128-key tile
+    (24, 17, 4, 2, 64),        # short prefix, head_dim 64
+    (96, 1000, 64, 8, 64),     # GPT-OSS heads (G = 8)
+    (8, 1, 8, 8, 128),         # one key, G = 1
+    (256, 4096, 32, 8, 128),   # several CTAs per head
+])
+@pytest.mark.parametrize("layout", ["nhd", "hnd"])
+def test_single_prefill_contiguous(cuda_device, N, P, Hq, Hk, D, layout):
+    import d2sd_b200 as d
+    g = torch.Generator().manual_seed(N * 7 + P)
+    q = rand((N, Hq, D), g, cuda_device)
+    k = rand((P, Hk, D), g, cuda_device)
+    v = rand((P, Hk, D), g, cuda_device)
+    kk, vv = (k, v) if layout == "nhd" else (k.transpose(0, 1).contiguous(),
+                                              v.transpose(0, 1).contiguous())
+    out, lse = d.single_prefill_with_kv_cache(q, kk, vv, causal=False, kv_layout=layout.upper(),
+                                              return_lse=True, sm_scale=D ** -0.5)
+    ro, rl = AT.single_prefill(f64(q), f64(k), f64(v), causal=False, sm_scale=D ** -0.5)
+    close(out, ro)
+    close(lse, rl, atol=LSE_ATOL)
+
+
+@pytest.mark.parametrize("page_order", ["identity", "shuffled"])
+@pytest.mark.parametrize("P,window", [(2048, None), (777, None), (1000, 128), (130, 128)])
+def test_cascade_paged(cuda_device, page_order, P, window):
+    import d2sd_b200 as d
+    B, T, Hq, Hk, D = 4, 16, 32, 8, 128
+    g = torch.Generator().manual_seed(P)
+    cache = d.PagedKVCache(1, Hk, D, max_tokens=P + 64, device=cuda_device,
+                           page_order=(torch.randperm(-(-(P + 64) // 16), generator=g)
+                                       if page_order == "shuffled" else None))
+    kp = rand((P, Hk, D), g, cuda_device)
+    vp = rand((P, Hk, D), g, cuda_device)
+    cache.write(0, kp, vp)
+    cache.length = P
+    q = rand((B, T, Hq, D), g, cuda_device)
+    kn = rand((B, T, Hk, D), g, cuda_device)
+    vn = rand((B, T, Hk, D), g, cuda_device)
+    kc, vc = cache.layer(0)
+    out, lse = d.cascade_attention(q, kn, vn, kc, vc, "paged_hnd", P, page_table=cache.page_table,
+                                   sliding_window=window)
+    ro, rl = AT.cascade_attention(f64(q), f64(kn), f64(vn), f64(kp), f64(vp), causal=True,
+                                  sliding_window=window)
+    close(out, ro)
+    close(lse, rl, atol=LSE_ATOL)
+
+
+@pytest.mark.parametrize("shared", [0, 4, 8])
+def test_cascade_tree_shared_trunk(cuda_device, shared):
+    """Branches sharing their first `shared` tokens: prefix attention runs on the
+    de-duplicated rows and must equal the per-branch result."""
+    import d2sd_b200 as d
+    B, T, Hq, Hk, D, P = 8, 32, 32, 8, 128, 1536
+    g = torch.Generator().manual_seed(11 + shared)
+    q = rand((B, T, Hq, D), g, cuda_device)
+    kn = rand((B, T, Hk, D), g, cuda_device)
+    vn = rand((B, T, Hk, D), g, cuda_device)
+    if shared:
+        q[:, :shared] = q[0:1, :shared]
+        kn[:, :shared] = kn[0:1, :shared]
+        vn[:, :shared] = vn[0:1, :shared]
+    kp = rand((P, Hk, D), g, cuda_device)
+    vp = rand((P, Hk, D), g, cuda_device)
+    out, lse = d.cascade_attention(q, kn, vn, kp, vp, "nhd", P, shared_tokens=shared)
+    ro, rl = AT.cascade_attention(f64(q), f64(kn), f64(vn), f64(kp), f64(vp), causal=True)
+    close(out, ro)
+    close(lse, rl, atol=LSE_ATOL)
+
+
+@pytest.mark.parametrize("sink_mode", ["reference", "exact"])
+def test_cascade_sinks_gptoss_shapes(cuda_device, sink_mode):
+    import d2sd_b200 as d
+    B, T, Hq, Hk, D, P = 6, 16, 64, 8, 64, 700
+    g = torch.Generator().manual_seed(5)
+    q = rand((B, T, Hq, D), g, cuda_device)
+    kn = rand((B, T, Hk, D), g, cuda_device)
+    vn = rand((B, T, Hk, D), g, cuda_device)
+    kp = rand((P, Hk, D), g, cuda_device)
+    vp = rand((P, Hk, D), g, cuda_device)
+    sinks = torch.randn(Hq, generator=g).to(cuda_device)
+    for window in (None, 128):
+        out, lse = d.cascade_attention(q, kn, vn, kp, vp, "nhd", P, sliding_window=window,
+                                       sinks=sinks, sink_mode=sink_mode)
+        ro, rl = AT.cascade_attention(f64(q), f64(kn), f64(vn), f64(kp), f64(vp), causal=True,
+                                      sliding_window=window, sinks=f64(sinks),
+                                      sink_mode=sink_mode)
+        close(out, ro)
+        close(lse, rl, atol=LSE_ATOL)
+
+
+def test_cascade_empty_prefix(cuda_device):
+    import d2sd_b200 as d
+    B, T, Hq, Hk, D = 2, 8, 8, 2, 64
+    g = torch.Generator().manual_seed(9)
+    q = rand((B, T, Hq, D), g, cuda_device)
+    kn = rand((B, T, Hk, D), g, cuda_device)
+    vn = rand((B, T, Hk, D), g, cuda_device)
+    kp = rand((16, Hk, D), g, cuda_device)
+    out, lse = d.cascade_attention(q, kn, vn, kp, kp, "nhd", 0)
+    ro, rl = AT.cascade_attention(f64(q), f64(kn), f64(vn), np.zeros((0, Hk, D)),
+                                  np.zeros((0, Hk, D)), causal=True)
+    close(out, ro)
+    close(lse, rl, atol=LSE_ATOL)
+
+
+def test_multi_request_plan(cuda_device):
+    """Batched serving shape: requests of different prefix lengths in one launch."""
+    import d2sd_b200 as d
+    from d2sd_b200 import ops
+    Hq, Hk, D, B, T = 32, 8, 128, 4, 16
+    g = torch.Generator().manual_seed(21)
+    lens = [512, 1333, 17, 4000, 256, 0, 129]
+    R = len(lens)
+    ps = 16
+    pages = [-(-L // ps) for L in lens]
+    total_pages = sum(pages) + 4
+    perm = torch.randperm(total_pages, generator=g)
+    pool_k = torch.zeros(total_pages, Hk, ps, D, dtype=torch.bfloat16, device=cuda_device)
+    pool_v = torch.zeros_like(pool_k)
+    table, offs, kps, vps = [], [], [], []
+    cur = 0
+    for L, npg in zip(lens, pages):
+        offs.append(len(table))
+        phys = perm[cur:cur + npg]
+        cur += npg
+        table += phys.tolist()
+        kp = rand((L, Hk, D), g, cuda_device)
+        vp = rand((L, Hk, D), g, cuda_device)
+        pos = torch.arange(L)
+        pool_k[phys[pos // ps].to(cuda_device), :, (pos % ps).to(cuda_device)] = kp
+        pool_v[phys[pos // ps].to(cuda_device), :, (pos % ps).to(cuda_device)] = vp
+        kps.append(kp)
+        vps.append(vp)
+    page_table = torch.tensor(table + [0], dtype=torch.int32, device=cuda_device)
+    q = rand((R * B * T, Hq, D), g, cuda_device)
+    reqs = [d.Request(B * T, r * B * T, 0, L, offs[r]) for r, L in enumerate(lens)]
+    plan = d.CascadePlan(reqs, Hq, Hk, D, cuda_device)
+    plan.run_prefix(q, pool_k, pool_v, "paged_hnd", D ** -0.5, page_table=page_table)
+    kn = rand((R * B * T, Hk, D), g, cuda_device)
+    vn = rand((R * B * T, Hk, D), g, cuda_device)
+    out = torch.empty_like(q)
+    lse = torch.empty(R * B * T, Hq, dtype=torch.float32, device=cuda_device)
+    ops.suffix_merge(q, kn, vn, out, lse, num_blocks=R * B, block_len=T, num_qo_heads=Hq,
+                     num_kv_heads=Hk, sm_scale=D ** -0.5, partial=plan.partial,
+                     plan_dev=plan.plan)
+    assert int(plan.status.item()) == 0
+    for r, L in enumerate(lens):
+        sl = slice(r * B * T, (r + 1) * B * T)
+        ro, rl = AT.cascade_attention(f64(q[sl]).reshape(B, T, Hq, D),
+                                      f64(kn[sl]).reshape(B, T, Hk, D),
+                                      f64(vn[sl]).reshape(B, T, Hk, D),
+                                      f64(kps[r]).reshape(L, Hk, D),
+                                      f64(vps[r]).reshape(L, Hk, D), causal=True)
+        close(out[sl].reshape(B, T, Hq, D), ro)
+        close(lse[sl].reshape(B, T, Hq), rl, atol=LSE_ATOL)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_runner_drop_in(cuda_device, causal):
+    """CascadeGraphRunner.run: merges the local attention into out/lse in place."""
+    import d2sd_b200 as d
+    B, T, Hq, Hk, D, P = 5, 32, 32, 8, 128, 640
+    g = torch.Generator().manual_seed(1 + causal)
+    r = d.CascadeGraphRunner(T, Hq, Hk, D, torch.bfloat16, cuda_device, D ** -0.5, causal)
+    for bsz in range(2, 6):
+        r._capture(bsz)
+    q = rand((B, T, Hq, D), g, cuda_device)
+    k = rand((B, T, Hk, D), g, cuda_device)
+    v = rand((B, T, Hk, D), g, cuda_device)
+    kp = rand((P, Hk, D), g, cuda_device)
+    vp = rand((P, Hk, D), g, cuda_device)
+    out_s, lse_s = d.single_prefill_with_kv_cache(q.reshape(B * T, Hq, D), kp, vp, causal=False,
+                                                  return_lse=True, sm_scale=D ** -0.5)
+    out_s = out_s.view(B, T, Hq, D)
+    lse_s = lse_s.view(B, T, Hq)
+    ref_in_o, ref_in_l = f64(out_s), f64(lse_s)
+    # non-contiguous k/v views as model/dflash.py:124 passes
+    kt = k.transpose(1, 2).contiguous().transpose(1, 2)
+    r.run(q, kt, v, out_s, lse_s)
+    ro, rl = AT.runner_local_merge(f64(q), f64(k), f64(v), ref_in_o, ref_in_l, causal, D ** -0.5)
+    close(out_s, ro)
+    close(lse_s, rl, atol=LSE_ATOL)
+    fo, fl = AT.cascade_attention(f64(q), f64(k), f64(v), f64(kp), f64(vp), causal=causal)
+    close(out_s, fo)
+
+
+def test_merge_state_in_place(cuda_device):
+    import d2sd_b200 as d
+    g = torch.Generator().manual_seed(3)
+    n, H, D = 50, 8, 128
+    v = rand((n, H, D), g, cuda_device)
+    vo = rand((n, H, D), g, cuda_device)
+    s = (torch.randn(n, H, generator=g) * 3).to(cuda_device)
+    so = (torch.randn(n, H, generator=g) * 3).to(cuda_device)
+    rv, rs = AT.merge_state(f64(v), f64(s), f64(vo), f64(so))
+    d.merge_state_in_place(v, s, vo, so)
+    close(v, rv)
+    close(s, rs, atol=1e-4)
+
+
+@pytest.mark.parametrize("kind", ["qwen3", "gptoss"])
+def test_reference_golden_attention(cuda_device, kind):
+    """The attention each layer of the reference's cascade_verify_forward fed
+    o_proj (tests/golden), recomputed by the kernels from bf16-rounded inputs."""
+    import d2sd_b200 as d
+    for lay in load_cases(f"attention_{kind}.npz"):
+        to = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(torch.bfloat16).to(cuda_device)  # noqa
+        q, kn, vn, kp, vp = (to(lay[k]) for k in ("q", "k_new", "v_new", "k_prefix", "v_prefix"))
+        window = int(lay["window"])
+        sinks = lay.get("sinks")
+        st = None if sinks is None else torch.from_numpy(sinks).float().to(cuda_device)
+        out, _ = d.cascade_attention(q, kn, vn, kp, vp, "nhd", kp.shape[0],
+                                     sliding_window=None if window < 0 else window, sinks=st)
+        # bf16-rounded inputs against the fp32 golden: within the bf16 tolerance
+        close(out, lay["out"])
+        ro, _ = AT.cascade_attention(f64(q), f64(kn), f64(vn), f64(kp), f64(vp), causal=True,
+                                     sliding_window=None if window < 0 else window,
+                                     sinks=sinks)
+        close(out, ro)

@@ -286,7 +286,8 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
               if a.shared else q[l].reshape(N, hq, D) for l in range(L)]
     out = torch.empty(N, hq, D, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(N, hq, dtype=torch.float32, device=dev)
-    gathered = torch.empty(world, N, hq, D, dtype=torch.bfloat16, device=dev) if world > 1 else None
+    gathered = (torch.empty(world * N, hq, D, dtype=torch.bfloat16, device=dev) if world > 1
+                else None)
     ver = d.Verifier(B, T, V, dev)
     new_k = kn.transpose(2, 3)  # [L, B, hk, T, D] views of the token-major K/V
     new_v = vn.transpose(2, 3)

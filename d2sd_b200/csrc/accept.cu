@@ -38,8 +38,8 @@ __device__ __forceinline__ bool better(float va, int64_t ia, float vb, int64_t i
 }
 
 __host__ __device__ inline int num_chunks_for(int64_t rows, int64_t vocab, int sms) {
-  // ~4 CTAs per SM over the whole grid, chunks of at least 8192 elements.
-  int64_t target = (static_cast<int64_t>(sms) * 4 + rows - 1) / rows;
+  // ~8 CTAs per SM over the whole grid, chunks of at least 8192 elements.
+  int64_t target = (static_cast<int64_t>(sms) * 8 + rows - 1) / rows;
   int64_t max_by_size = (vocab + 8191) / 8192;
   int64_t c = target < max_by_size ? target : max_by_size;
   if (c < 1) c = 1;
@@ -89,6 +89,48 @@ struct Vec<__half> {
   static constexpr int N = 8;
 };
 
+// NaN-propagating maximum of the elements of one 16-byte vector.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+template <typename T>
+struct VecMax;
+template <>
+struct VecMax<float> {
+  static __device__ __forceinline__ float max(const uint4& v) {
+    return max_nan(max_nan(__uint_as_float(v.x), __uint_as_float(v.y)),
+                   max_nan(__uint_as_float(v.z), __uint_as_float(v.w)));
+  }
+};
+__device__ __forceinline__ uint32_t max_nan_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_nan_f16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+template <>
+struct VecMax<__nv_bfloat16> {
+  static __device__ __forceinline__ float max(const uint4& v) {
+    const uint32_t m = max_nan_bf16x2(max_nan_bf16x2(v.x, v.y), max_nan_bf16x2(v.z, v.w));
+    // bf16 -> f32 is a shift of the bit pattern
+    return max_nan(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u));
+  }
+};
+template <>
+struct VecMax<__half> {
+  static __device__ __forceinline__ float max(const uint4& v) {
+    const uint32_t m = max_nan_f16x2(max_nan_f16x2(v.x, v.y), max_nan_f16x2(v.z, v.w));
+    const __half2 h = *reinterpret_cast<const __half2*>(&m);
+    return max_nan(__low2float(h), __high2float(h));
+  }
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
     accept_kernel(const T* __restrict__ logits, int B, int TB, int64_t V, int64_t s_b,
@@ -107,9 +149,11 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t c0 = static_cast<int64_t>(chunk) * csize;
   const int64_t c1 = c0 + csize < V ? c0 + csize : V;
 
-  // Per-thread scan in increasing index order: a strict ">" keeps the first
-  // maximal index; NaN (never ">") is tracked separately and resolved by a
-  // rescan of this thread's elements, which only runs when a NaN was seen.
+  // Per-thread scan in increasing index order. Each 16-byte vector is reduced
+  // with a NaN-propagating max first; only a vector that beats the running best
+  // (or holds a NaN) is searched for its first maximal index. A strict ">"
+  // keeps the first index among equal maxima; once the best is NaN nothing
+  // replaces it (torch.argmax: the first NaN wins).
   float best_v = -INFINITY;
   int64_t best_i = INT64_MAX;
   if (c0 < c1) {
@@ -117,71 +161,40 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t nvec = vec_ok ? (c1 - c0) / VN : 0;
     const int64_t tail0 = c0 + nvec * VN;
     const uint4* src = reinterpret_cast<const uint4*>(base + c0);
-    bool has_nan = false;
-    int64_t first_idx = INT64_MAX;  // first element this thread looks at
-    if (threadIdx.x < nvec) first_idx = c0 + static_cast<int64_t>(threadIdx.x) * VN;
+    if (threadIdx.x < nvec) best_i = c0 + static_cast<int64_t>(threadIdx.x) * VN;
+    auto visit = [&](const uint4& raw, int64_t first) {
+      const float vm = VecMax<T>::max(raw);
+      if (!(vm <= best_v) && best_v == best_v) {
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int k = 0; k < VN; ++k) {
+          const float x = Num<T>::to_f(e[k]);
+          if (x != x || x == vm) {
+            best_v = x;
+            best_i = first + k;
+            break;
+          }
+        }
+      }
+    };
     int64_t vI = threadIdx.x;
     for (; vI + 3 * kThreads < nvec; vI += 4 * kThreads) {
       uint4 raw[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) raw[u] = __ldg(src + vI + u * kThreads);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const T* e = reinterpret_cast<const T*>(&raw[u]);
-#pragma unroll
-        for (int k = 0; k < VN; ++k) {
-          const float x = Num<T>::to_f(e[k]);
-          if (x > best_v) {
-            best_v = x;
-            best_i = c0 + (vI + u * kThreads) * VN + k;
-          }
-          has_nan |= (x != x);
-        }
-      }
+      for (int u = 0; u < 4; ++u) visit(raw[u], c0 + (vI + u * kThreads) * VN);
     }
-    for (; vI < nvec; vI += kThreads) {
-      uint4 raw = __ldg(src + vI);
-      const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-      for (int k = 0; k < VN; ++k) {
-        const float x = Num<T>::to_f(e[k]);
-        if (x > best_v) {
-          best_v = x;
-          best_i = c0 + vI * VN + k;
-        }
-        has_nan |= (x != x);
-      }
-    }
+    for (; vI < nvec; vI += kThreads) visit(__ldg(src + vI), c0 + vI * VN);
     for (int64_t j = tail0 + threadIdx.x; j < c1; j += kThreads) {
-      if (first_idx == INT64_MAX) first_idx = j;
       const float x = Num<T>::to_f(base[j]);
-      if (x > best_v) {
+      if (best_i == INT64_MAX) {
+        best_v = x;
+        best_i = j;
+      } else if ((x > best_v || (x != x)) && best_v == best_v) {
         best_v = x;
         best_i = j;
       }
-      has_nan |= (x != x);
-    }
-    if (best_i == INT64_MAX) best_i = first_idx;  // all -inf: first index seen
-    if (has_nan) {
-      // first NaN among this thread's elements (same visiting order as above)
-      int64_t nan_i = INT64_MAX;
-      for (int64_t w = threadIdx.x; w < nvec && nan_i == INT64_MAX; w += kThreads) {
-        uint4 raw = __ldg(src + w);
-        const T* e = reinterpret_cast<const T*>(&raw);
-        for (int k = 0; k < VN; ++k) {
-          const float x = Num<T>::to_f(e[k]);
-          if (x != x) {
-            nan_i = c0 + w * VN + k;
-            break;
-          }
-        }
-      }
-      for (int64_t j = tail0 + threadIdx.x; j < c1 && nan_i == INT64_MAX; j += kThreads) {
-        const float x = Num<T>::to_f(base[j]);
-        if (x != x) nan_i = j;
-      }
-      best_v = __int_as_float(0x7fc00000);
-      best_i = nan_i;
     }
   }
   // block reduce

@@ -22,10 +22,6 @@
 // as packed bf16 over the first 64 columns of S_i.
 // The two tiles ping-pong: while warpgroup 0 turns S0 into P0 the tensor core
 // runs Q1 K^T and P1 V, and vice versa.
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
 #include "common.cuh"
 #include "plan_layout.h"
 
@@ -283,60 +279,69 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
       if (!warp_wait(&bars[C::B_SFULL + i], scount & 1, abort)) return;
       ++scount;
       tc_fence_after();
-      uint32_t s[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32_wait(lane_base + s_col(i) + c * 32, s[c]);
+      uint32_t s[128];
+      tmem_ld128_wait(lane_base + s_col(i), s);
       const int pos0 = t * kTileKeys;
-      const bool edge = pos0 < kv_start || pos0 + kTileKeys > kv_end;
-      float mx = -INFINITY;
+      if (pos0 < kv_start || pos0 + kTileKeys > kv_end) {  // edge tile: mask invisible keys
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float v = __uint_as_float(s[c][e]);
-          if (edge) {
-            const int pos = pos0 + c * 32 + e;
-            if (pos < kv_start || pos >= kv_end) v = -INFINITY;
-            s[c][e] = __float_as_uint(v);
-          }
-          mx = fmaxf(mx, v);
+        for (int e = 0; e < 128; ++e) {
+          const int pos = pos0 + e;
+          if (pos < kv_start || pos >= kv_end) s[e] = 0xff800000u;  // -inf
         }
       }
-      const float m_tile = mx * sl2;
+      // row max with 8 independent accumulators (short dependency chains)
+      float mx[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx[e] = __uint_as_float(s[e]);
+#pragma unroll
+      for (int e = 8; e < 128; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(s[e]));
+#pragma unroll
+      for (int w = 4; w > 0; w >>= 1) {
+#pragma unroll
+        for (int e = 0; e < w; ++e) mx[e] = fmaxf(mx[e], mx[e + w]);
+      }
+      const float m_tile = mx[0] * sl2;
+      // lazy max: keep m_run unless this tile's max exceeds it by more than 8
+      // (p <= 2^8 then); when it does, O and l are rescaled by 2^(m_old - m_new)
+      // below, after P is written (S registers are free by then)
+      float f = 1.f;
       if (t == t0) {
         m_run = m_tile;
       } else if (m_tile > m_run + 8.f) {
-        const float f = fast_exp2(m_run - m_tile);
-        l_run *= f;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32_wait(lane_base + o_col(i) + c * 32, o);
-          uint32_t lo[16], hi[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            lo[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-            hi[e] = __float_as_uint(__uint_as_float(o[16 + e]) * f);
-          }
-          tmem_st16(lane_base + o_col(i) + c * 32, lo);
-          tmem_st16(lane_base + o_col(i) + c * 32 + 16, hi);
-        }
+        f = fast_exp2(m_run - m_tile);
         m_run = m_tile;
       }
       const float neg_m = -m_run;
-      float sum = 0.f;
+      float sm[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sm[e] = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c][2 * e]), sl2, neg_m));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c][2 * e + 1]), sl2, neg_m));
-          sum += p0 + p1;
+          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, neg_m));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, neg_m));
+          sm[(2 * e) & 7] += p0;
+          sm[(2 * e + 1) & 7] += p1;
           pk[e] = pack_bf16x2(p0, p1);
         }
         tmem_st16(lane_base + s_col(i) + c * 16, pk);
       }
+      if (f != 1.f) {
+        // O holds the sum up to the previous tile: this tile's S commit follows
+        // the previous P.V in issue order, so that P.V has completed
+        l_run *= f;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32_wait(lane_base + o_col(i) + c * 32, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+          tmem_st32(lane_base + o_col(i) + c * 32, o);
+        }
+      }
+      const float sum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
       l_run += sum;
       tmem_st_wait();
       tc_fence_before();
@@ -372,7 +377,7 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
 }
 
 template <int D>
-__global__ void __launch_bounds__(kNumThreads, 1)
+__global__ void __maxnreg__(200)
     prefix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v, const PrefixParams p) {
@@ -443,38 +448,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult qres;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
-                                         &qres) == cudaSuccess &&
-        qres == cudaDriverEntryPointSuccess) {
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-    }
-  });
-  return fn;
-}
-
-int encode_bf16_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                    const uint64_t* strides_bytes, const uint32_t* box, const char* what) {
-  auto fn = get_encode_fn();
-  if (!fn) return fail(D2SD_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  uint32_t estr[5] = {1, 1, 1, 1, 1};
-  CUresult res = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims,
-                    strides_bytes, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (res != CUDA_SUCCESS) {
-    return fail(D2SD_ERR_INVALID_ARGUMENT,
-                std::string("cuTensorMapEncodeTiled failed for ") + what + " (CUresult " +
-                    std::to_string(static_cast<int>(res)) + ")");
-  }
-  return D2SD_OK;
-}
-
 template <int D>
 int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
            const PrefixParams& prm, int num_ctas, cudaStream_t stream) {
@@ -540,7 +513,7 @@ extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int6
     const uint64_t strides[2] = {static_cast<uint64_t>(q_stride_head) * 2,
                                  static_cast<uint64_t>(q_stride_token) * 2};
     const uint32_t box[3] = {64, static_cast<uint32_t>(G), static_cast<uint32_t>(plan::kTileRows / G)};
-    int rc = encode_bf16_map(&tq, q, 3, dims, strides, box, "q");
+    int rc = encode_tensor_map(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 3, dims, strides, box, "q");
     if (rc) return rc;
   }
   int rows_per_box;
@@ -571,9 +544,9 @@ extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int6
     box[1] = static_cast<uint32_t>(rows_per_box);
     box[2] = 1;
     box[3] = 1;
-    int rc = encode_bf16_map(&tk, k, 4, dims, strides, box, "k");
+    int rc = encode_tensor_map(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, 4, dims, strides, box, "k");
     if (rc) return rc;
-    rc = encode_bf16_map(&tv, v, 4, dims, strides, box, "v");
+    rc = encode_tensor_map(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, v, 4, dims, strides, box, "v");
     if (rc) return rc;
   }
   PrefixParams prm;

@@ -5,16 +5,23 @@
 // Reference: CascadeGraphRunner._capture/_run_local_merge
 // (model/cascade_graph.py:52-60) runs, per branch i, a causal (verify) or full
 // (DTA, model/dflash.py:127-133) single_prefill over the branch's own block
-// tokens and then merge_state_in_place into the level-1 state; the sink rescale
+// tokens, then merge_state_in_place into the level-1 state; the sink rescale
 // out *= sigmoid(lse - sink) follows at generation/verification.py:173-176.
-// Here one launch does all branches: a CTA owns (block, kv head, row chunk),
-// stages the block's K/V of that head in shared memory once, and every warp
-// walks its query rows (token t, query head g of the group): lane j scores key
-// j (and j+32), the warp reduces max/sum with shuffles, lanes own D/32 output
-// columns for P.V, and the row is merged in registers with every prefix
-// partial state (or with a dense prefix state) before one store.
+//
+// One launch covers every branch. A CTA owns (block, kv head, 128-row tile);
+// rows are token*G + g, the G query heads of the kv head, so the whole GQA
+// group shares one K/V tile. Thread 0 TMA-loads the Q tile and the block's K
+// and V (128-byte swizzle) and issues S = Q K^T on tcgen05 into TMEM
+// (M=128, N=32 or 64 keys); each thread (= TMEM lane = row) masks (causal,
+// full or a custom bitmask), exponentiates and writes P back to TMEM as
+// 16-bit pairs; thread 0 issues O = P V (A from TMEM, V MN-major). The
+// epilogue reads O from TMEM 32 columns at a time and merges it with every
+// partial state kernel (a) wrote for the row's query tile (or with a dense
+// prefix state), applies the sink factor and stores the row once.
 #include "common.cuh"
 #include "plan_layout.h"
+
+#include <cstring>
 
 namespace d2sd {
 namespace {
@@ -22,20 +29,12 @@ namespace {
 using namespace plan;
 
 constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / 32;
-constexpr int kRowsPerCta = 32;
 constexpr int kMaxBlockLen = 64;
+constexpr int kPanelQ = 128 * 128;  // 128 rows x 128 bytes
 
 struct SuffixParams {
-  const void* q;
-  int64_t q_st, q_sh;
-  const void* k;
-  const void* v;
-  int64_t kv_st, kv_sh;
-  int32_t num_blocks, block_len, mask_mode;
-  const uint64_t* custom_mask;
-  const float* partial;
   const int32_t* plan;
+  const float* partial;
   const int32_t* prefix_token;
   const void* prefix_out;
   int64_t po_st, po_sh;
@@ -46,206 +45,307 @@ struct SuffixParams {
   float* lse;
   int64_t l_st;
   const float* sinks;
-  int32_t sink_mode;
-  int32_t Hq, Hk, G;
+  const uint64_t* custom_mask;
+  int32_t* status;
+  int32_t has_local;
+  int32_t block_len, mask_mode, sink_mode;
+  int32_t Hq, G;
   float scale_log2;
 };
 
-template <int DPL>
-struct RowState {
-  float lse;
-  float o[DPL];
+template <int D, int NK>
+struct SCfg {
+  static constexpr int kPanels = D / 64;
+  static constexpr int kPanelKV = NK * 128;
+  static constexpr int kQBytes = 128 * D * 2;
+  static constexpr int kKVBytes = NK * D * 2;
+  static constexpr int kSmemQ = 0;
+  static constexpr int kSmemK = kQBytes;
+  static constexpr int kSmemV = kSmemK + kKVBytes;
+  static constexpr int kSmemBar = kSmemV + kKVBytes;
+  static constexpr int kSmemBytes = kSmemBar + 64 + 1024;
 };
 
-template <int DPL>
-__device__ __forceinline__ void merge_into(RowState<DPL>& a, float lse_b, const float (&ob)[DPL]) {
-  if (lse_b == -INFINITY) return;
-  if (a.lse == -INFINITY) {
-    a.lse = lse_b;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) a.o[e] = ob[e];
-    return;
+template <typename T>
+struct Fmt;
+template <>
+struct Fmt<__nv_bfloat16> {
+  static constexpr uint32_t kUmma = 1;
+  static __device__ __forceinline__ uint32_t pack(float a, float b) { return pack_bf16x2(a, b); }
+};
+template <>
+struct Fmt<__half> {
+  static constexpr uint32_t kUmma = 0;
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
   }
-  const float M = fmaxf(a.lse, lse_b);
-  const float wa = fast_exp2(a.lse - M), wb = fast_exp2(lse_b - M);
-  const float inv = 1.f / (wa + wb);
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) a.o[e] = (wa * a.o[e] + wb * ob[e]) * inv;
-  a.lse = M + fast_log2(wa + wb);
+};
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) {
+    while (!mbar_try_wait(bar, parity)) {
+    }
+  }
+  return ok != 0;
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads) suffix_merge_kernel(const SuffixParams p) {
-  constexpr int DPL = D / 32;  // output columns per lane
-  constexpr int KP = D + 2;    // padded K row (elements): conflict-free lane-per-key reads
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  T* ks = reinterpret_cast<T*>(smem_raw);
-  T* vs = ks + kMaxBlockLen * KP;
-  float* qbuf = reinterpret_cast<float*>(vs + kMaxBlockLen * D);
+template <typename T, int D, int NK>
+__global__ void __launch_bounds__(kThreads)
+    suffix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                            const __grid_constant__ CUtensorMap tm_k,
+                            const __grid_constant__ CUtensorMap tm_v, const SuffixParams p) {
+  using C = SCfg<D, NK>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSmemBar);  // load, S, O
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int blk = blockIdx.x, h = blockIdx.y;
+  const int blk = blockIdx.x, h = blockIdx.y, rt = blockIdx.z;
   const int TB = p.block_len, G = p.G;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const bool has_local = p.k != nullptr;
+  const int warp = threadIdx.x / 32;
+  const int R = rt * 128 + threadIdx.x;
+  const int t = R / G, g = R - (R / G) * G;
+  const bool valid = t < TB;
+  const int tok = blk * TB + t;
+  const int hq = h * G + g;
+  const float sl2 = p.scale_log2;
 
-  if (has_local) {
-    const T* kg = static_cast<const T*>(p.k);
-    const T* vg = static_cast<const T*>(p.v);
-    for (int idx = threadIdx.x; idx < TB * D; idx += kThreads) {
-      const int j = idx / D, d = idx % D;
-      const int64_t off = (static_cast<int64_t>(blk) * TB + j) * p.kv_st + h * p.kv_sh + d;
-      ks[j * KP + d] = kg[off];
-      vs[j * D + d] = vg[off];
+  float lse_l = -INFINITY, inv_l = 0.f;
+  uint32_t tmem = 0;
+  bool ok = true;
+  if (p.has_local) {
+    if (threadIdx.x == 0) {
+      for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
+      *abort = 0;
+      fence_mbar_init();
+      fence_proxy_async_smem();
+    }
+    if (warp == 0) {
+      tmem_alloc(tmem_slot, 256);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem = *tmem_slot;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&bars[0], C::kQBytes + 2 * C::kKVBytes);
+#pragma unroll
+      for (int pn = 0; pn < C::kPanels; ++pn) {
+        tma_load_3d(smem + C::kSmemQ + pn * kPanelQ, &tm_q, &bars[0], pn * 64, h * G,
+                    blk * TB + rt * (128 / G));
+        tma_load_3d(smem + C::kSmemK + pn * C::kPanelKV, &tm_k, &bars[0], pn * 64, h, blk * TB);
+        tma_load_3d(smem + C::kSmemV + pn * C::kPanelKV, &tm_v, &bars[0], pn * 64, h, blk * TB);
+      }
+      if (mbar_wait(&bars[0], 0, abort)) {
+        tc_fence_after();
+        constexpr uint32_t idesc = umma_idesc(128, NK, false, Fmt<T>::kUmma);
+        const uint32_t a0 = smem_u32(smem + C::kSmemQ);
+        const uint32_t b0 = smem_u32(smem + C::kSmemK);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t ka = (ks / 4) * kPanelQ + (ks % 4) * 32;
+          const uint32_t kb = (ks / 4) * C::kPanelKV + (ks % 4) * 32;
+          umma_ss(tmem, umma_desc_sw128(a0 + ka, 16, 1024), umma_desc_sw128(b0 + kb, 16, 1024),
+                  idesc, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[1]);
+      }
+    }
+    ok = warp_wait(&bars[1], 0, abort);
+    float l = 0.f, m = -INFINITY;
+    if (ok) {
+      tc_fence_after();
+      uint32_t s[NK];
+      tmem_ld32_wait(lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      if (NK == 64) tmem_ld32_wait(lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 % NK]));
+      uint64_t allowed = 0;
+      if (valid) {
+        if (p.mask_mode == D2SD_MASK_CAUSAL) allowed = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
+        else if (p.mask_mode == D2SD_MASK_CUSTOM) allowed = p.custom_mask[tok];
+        else allowed = ~0ull;
+        if (TB < 64) allowed &= (1ull << TB) - 1ull;
+      }
+#pragma unroll
+      for (int j = 0; j < NK; ++j) {
+        if (!((allowed >> j) & 1ull)) s[j] = 0xff800000u;
+        m = fmaxf(m, __uint_as_float(s[j]));
+      }
+      const float mm = (m == -INFINITY) ? 0.f : m * sl2;
+#pragma unroll
+      for (int c = 0; c < NK / 32; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, -mm));
+          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, -mm));
+          l += p0 + p1;
+          pk[e] = Fmt<T>::pack(p0, p1);
+        }
+        tmem_st16(lane_base + c * 16, pk);
+      }
+      tmem_st_wait();
+      if (l > 0.f) {
+        lse_l = mm + fast_log2(l);
+        inv_l = 1.f / l;
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0 && ok && !*abort) {
+      tc_fence_after();
+      constexpr uint32_t idesc = umma_idesc(128, D, true, Fmt<T>::kUmma);
+      const uint32_t b0 = smem_u32(smem + C::kSmemV);
+#pragma unroll
+      for (int ks = 0; ks < NK / 16; ++ks) {
+        umma_ts(tmem + 128, tmem + ks * 8, umma_desc_sw128(b0 + ks * 16 * 128, C::kPanelKV, 1024),
+                idesc, ks > 0 ? 1u : 0u);
+      }
+      umma_commit(&bars[2]);
+    }
+    ok = ok && warp_wait(&bars[2], 0, abort);
+    tc_fence_after();
+  }
+
+  // ---- prefix states: their LSEs first (max and denominator) ----
+  int slot_base = 0, nslots = 0;
+  const T* po = nullptr;
+  float lse_p = -INFINITY;
+  if (valid && p.partial) {
+    const int32_t* pl = p.plan;
+    const int ptok = p.prefix_token ? p.prefix_token[tok] : tok;
+    const int req = (ptok >= 0 && ptok < pl[H_NUM_TOKENS]) ? pl[pl[H_OFF_TOKENS] + ptok] : -1;
+    if (req >= 0) {
+      const int32_t* rq = pl + pl[H_OFF_REQUESTS] + req * kReqInts;
+      const int qrow = (ptok - rq[2]) * G + g;
+      const int32_t* un = pl + pl[H_OFF_UNITS] + (rq[0] + h * rq[1] + qrow / kTileRows) * kUnitInts;
+      slot_base = un[0] * kTileRows + (qrow % kTileRows);  // row index into the slot array
+      nslots = un[1];
+    }
+  } else if (valid && p.prefix_out) {
+    po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(tok) * p.po_st +
+         static_cast<int64_t>(hq) * p.po_sh;
+    lse_p = p.prefix_lse[static_cast<int64_t>(tok) * p.pl_st + hq];
+  }
+  const int64_t slot_floats = static_cast<int64_t>(kTileRows) * (D + 1);
+  // slot_base = slot*128 + prow; the row's O starts at slot*slot_floats + prow*D
+  auto slot_row = [&](int s) -> int64_t {
+    const int64_t idx = slot_base + static_cast<int64_t>(s) * kTileRows;
+    return (idx / kTileRows) * slot_floats + (idx % kTileRows) * D;
+  };
+  auto slot_lse = [&](int s) -> float {
+    const int64_t idx = slot_base + static_cast<int64_t>(s) * kTileRows;
+    return p.partial[(idx / kTileRows) * slot_floats + kTileRows * D + (idx % kTileRows)];
+  };
+  float M = lse_l;
+  for (int s = 0; s < nslots; ++s) M = fmaxf(M, slot_lse(s));
+  M = fmaxf(M, lse_p);
+  const float Mz = (M == -INFINITY) ? 0.f : M;
+  const float w_l = (lse_l == -INFINITY) ? 0.f : fast_exp2(lse_l - Mz);
+  const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
+  float den = w_l + w_p;
+  for (int s = 0; s < nslots; ++s) {
+    const float ls = slot_lse(s);
+    den += (ls == -INFINITY) ? 0.f : fast_exp2(ls - Mz);
+  }
+  const float lse_out = den > 0.f ? Mz + fast_log2(den) : -INFINITY;
+  float factor = den > 0.f ? 1.f / den : 0.f;
+  if (p.sinks && p.sink_mode != D2SD_SINK_NONE && valid) {
+    const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse_out * kLn2 : lse_out) - p.sinks[hq];
+    factor *= 1.f / (1.f + __expf(-x));
+  }
+  const float wl = w_l * inv_l;  // local O is unnormalised in TMEM
+
+  // ---- epilogue, 32 columns at a time ----
+  T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(tok) * p.o_st +
+            static_cast<int64_t>(hq) * p.o_sh;
+#pragma unroll 1
+  for (int c = 0; c < D / 32; ++c) {
+    float o[32];
+    if (p.has_local) {
+      uint32_t r[32];
+      tmem_ld32_wait(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 128 + c * 32, r);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = ok ? __uint_as_float(r[e]) * wl : 0.f;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) o[e] = 0.f;
+    }
+    if (valid) {
+      for (int s = 0; s < nslots; ++s) {
+        const float ls = slot_lse(s);
+        if (ls == -INFINITY) continue;
+        const float w = fast_exp2(ls - Mz);
+        const float4* src = reinterpret_cast<const float4*>(p.partial + slot_row(s) + c * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float4 v = src[e];
+          o[4 * e] = fmaf(w, v.x, o[4 * e]);
+          o[4 * e + 1] = fmaf(w, v.y, o[4 * e + 1]);
+          o[4 * e + 2] = fmaf(w, v.z, o[4 * e + 2]);
+          o[4 * e + 3] = fmaf(w, v.w, o[4 * e + 3]);
+        }
+      }
+      if (po) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = fmaf(w_p, Num<T>::to_f(po[c * 32 + e]), o[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        const uint32_t pr = Fmt<T>::pack(o[e] * factor, o[e + 1] * factor);
+        *reinterpret_cast<uint32_t*>(orow + c * 32 + e) = pr;
+      }
     }
   }
-  __syncthreads();
+  if (valid && p.lse) p.lse[static_cast<int64_t>(tok) * p.l_st + hq] = lse_out;
 
-  const int rows = TB * G;
-  const int row_end = min(rows, static_cast<int>(blockIdx.z + 1) * kRowsPerCta);
-  float* qw = qbuf + warp * D;
-  const T* qg = static_cast<const T*>(p.q);
-
-  for (int r = blockIdx.z * kRowsPerCta + warp; r < row_end; r += kWarps) {
-    const int t = r / G, g = r % G;
-    const int tok = blk * TB + t;
-    const int hq = h * G + g;
-    RowState<DPL> st;
-    st.lse = -INFINITY;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) st.o[e] = 0.f;
-
-    if (has_local) {
-      // q row -> per-warp buffer (fp32)
-      const T* qrow = qg + static_cast<int64_t>(tok) * p.q_st + static_cast<int64_t>(hq) * p.q_sh;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) qw[lane * DPL + e] = Num<T>::to_f(qrow[lane * DPL + e]);
-      __syncwarp();
-      uint64_t allowed;
-      if (p.mask_mode == D2SD_MASK_CAUSAL) {
-        allowed = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
-      } else if (p.mask_mode == D2SD_MASK_CUSTOM) {
-        allowed = p.custom_mask[tok];
-      } else {
-        allowed = ~0ull;
-      }
-      if (TB < 64) allowed &= (1ull << TB) - 1ull;
-      float sc[2];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int j = lane + half * 32;
-        sc[half] = -INFINITY;
-        if (j < TB && ((allowed >> j) & 1ull)) {
-          const T* kr = ks + j * KP;
-          float acc = 0.f;
-#pragma unroll 8
-          for (int d = 0; d < D; d += 2) {
-            acc = fmaf(qw[d], Num<T>::to_f(kr[d]), acc);
-            acc = fmaf(qw[d + 1], Num<T>::to_f(kr[d + 1]), acc);
-          }
-          sc[half] = acc * p.scale_log2;
-        }
-      }
-      float m = fmaxf(sc[0], sc[1]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      float pj[2];
-      pj[0] = sc[0] == -INFINITY ? 0.f : fast_exp2(sc[0] - m);
-      pj[1] = sc[1] == -INFINITY ? 0.f : fast_exp2(sc[1] - m);
-      float l = pj[0] + pj[1];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-      if (l > 0.f) {
-        float acc[DPL];
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[e] = 0.f;
-        const int jmax = TB < 32 ? TB : 32;
-        for (int j = 0; j < jmax; ++j) {
-          const float pv = __shfl_sync(0xffffffffu, pj[0], j);
-          const T* vr = vs + j * D + lane * DPL;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[e] = fmaf(pv, Num<T>::to_f(vr[e]), acc[e]);
-        }
-        for (int j = 32; j < TB; ++j) {
-          const float pv = __shfl_sync(0xffffffffu, pj[1], j - 32);
-          const T* vr = vs + j * D + lane * DPL;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[e] = fmaf(pv, Num<T>::to_f(vr[e]), acc[e]);
-        }
-        const float inv = 1.f / l;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) st.o[e] = acc[e] * inv;
-        st.lse = m + fast_log2(l);
-      }
-      __syncwarp();
+  if (p.has_local) {
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+      tc_fence_after();
+      tmem_dealloc(tmem, 256);
     }
-
-    // ---- prefix state ----
-    if (p.partial) {
-      const int32_t* pl = p.plan;
-      const int ptok = p.prefix_token ? p.prefix_token[tok] : tok;
-      const int ntok = pl[H_NUM_TOKENS];
-      const int req = (ptok >= 0 && ptok < ntok) ? pl[pl[H_OFF_TOKENS] + ptok] : -1;
-      if (req >= 0) {
-        const int32_t* rq = pl + pl[H_OFF_REQUESTS] + req * kReqInts;
-        const int nr = ptok - rq[2];
-        const int qrow = nr * G + g;
-        const int unit = rq[0] + h * rq[1] + qrow / kTileRows;
-        const int32_t* un = pl + pl[H_OFF_UNITS] + unit * kUnitInts;
-        const int prow = qrow % kTileRows;
-        const int64_t slot_floats = static_cast<int64_t>(kTileRows) * (D + 1);
-        for (int s = 0; s < un[1]; ++s) {
-          const float* sp = p.partial + static_cast<int64_t>(un[0] + s) * slot_floats;
-          const float lse_s = sp[kTileRows * D + prow];
-          float ob[DPL];
-          const float* orow = sp + prow * D + lane * DPL;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) ob[e] = orow[e];
-          merge_into<DPL>(st, lse_s, ob);
-        }
-      }
-    } else if (p.prefix_out) {
-      const T* po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(tok) * p.po_st +
-                    static_cast<int64_t>(hq) * p.po_sh + lane * DPL;
-      const float lse_p = p.prefix_lse[static_cast<int64_t>(tok) * p.pl_st + hq];
-      float ob[DPL];
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) ob[e] = Num<T>::to_f(po[e]);
-      merge_into<DPL>(st, lse_p, ob);
-    }
-
-    float factor = 1.f;
-    if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
-      const float x = (p.sink_mode == D2SD_SINK_EXACT ? st.lse * kLn2 : st.lse) - p.sinks[hq];
-      factor = 1.f / (1.f + __expf(-x));
-    }
-    T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(tok) * p.o_st +
-              static_cast<int64_t>(hq) * p.o_sh + lane * DPL;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) orow[e] = Num<T>::from_f(st.o[e] * factor);
-    if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(tok) * p.l_st + hq] = st.lse;
+    if (threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
   }
 }
 
-template <typename T, int D>
-int launch_suffix(const SuffixParams& prm, cudaStream_t stream) {
-  constexpr int KP = D + 2;
-  const size_t smem =
-      sizeof(T) * (kMaxBlockLen * KP + kMaxBlockLen * D) + sizeof(float) * kWarps * D;
+template <typename T, int D, int NK>
+int launch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                  const SuffixParams& prm, dim3 grid, cudaStream_t stream) {
+  using C = SCfg<D, NK>;
   static int configured = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured != dev) {
-    cudaError_t e = cudaFuncSetAttribute(suffix_merge_kernel<T, D>,
+    cudaError_t e = cudaFuncSetAttribute(suffix_attention_kernel<T, D, NK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
+                                         C::kSmemBytes);
     if (e != cudaSuccess)
       return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured = dev;
   }
-  const int rows = prm.block_len * prm.G;
-  dim3 grid(prm.num_blocks, prm.Hk, (rows + kRowsPerCta - 1) / kRowsPerCta);
-  suffix_merge_kernel<T, D><<<grid, kThreads, smem, stream>>>(prm);
-  return check_launch("suffix_merge_kernel");
+  const int smem = prm.has_local ? C::kSmemBytes : 0;
+  suffix_attention_kernel<T, D, NK><<<grid, kThreads, smem, stream>>>(tq, tk, tv, prm);
+  return check_launch("suffix_attention_kernel");
+}
+
+template <typename T>
+int dispatch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                    const SuffixParams& prm, int D, int NK, dim3 grid, cudaStream_t st) {
+  if (D == 128) {
+    return NK == 32 ? launch_suffix<T, 128, 32>(tq, tk, tv, prm, grid, st)
+                    : launch_suffix<T, 128, 64>(tq, tk, tv, prm, grid, st);
+  }
+  return NK == 32 ? launch_suffix<T, 64, 32>(tq, tk, tv, prm, grid, st)
+                  : launch_suffix<T, 64, 64>(tq, tk, tv, prm, grid, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -296,18 +396,22 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
                                  void* out, int64_t out_stride_token, int64_t out_stride_head,
                                  float* lse, int64_t lse_stride_token, const float* sinks,
                                  int32_t sink_mode, int32_t num_qo_heads, int32_t num_kv_heads,
-                                 int32_t head_dim, int32_t dtype, float sm_scale, void* stream) {
+                                 int32_t head_dim, int32_t dtype, float sm_scale,
+                                 int32_t* status, void* stream) {
   using namespace d2sd;
   if (!out || num_blocks < 0 || block_len <= 0 || num_qo_heads <= 0 || num_kv_heads <= 0 ||
       num_qo_heads % num_kv_heads != 0)
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: invalid argument");
   if (num_blocks == 0) return D2SD_OK;
-  if (block_len > kMaxBlockLen)
-    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: block_len must be <= 64");
+  const int G = num_qo_heads / num_kv_heads;
+  if (plan::kTileRows % G != 0)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: qo heads per kv head must divide 128");
   if ((k_local == nullptr) != (v_local == nullptr))
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: k_local and v_local go together");
   if (k_local && !q)
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: q is required with k_local");
+  if (k_local && block_len > kMaxBlockLen)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: block_len must be <= 64");
   if (mask_mode == D2SD_MASK_CUSTOM && !custom_mask)
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: custom mask pointer missing");
   if (mask_mode < D2SD_MASK_NONE || mask_mode > D2SD_MASK_CUSTOM)
@@ -318,22 +422,19 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: dense prefix needs its lse");
   if (head_dim != 64 && head_dim != 128)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: head_dim must be 64 or 128");
+  if (dtype != D2SD_DTYPE_BF16 && dtype != D2SD_DTYPE_F16)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: dtype must be bf16 or f16");
+  if ((out_stride_head % 2) || (out_stride_token % 2) ||
+      (reinterpret_cast<uintptr_t>(out) & 3u))
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: out rows must be 4-byte aligned");
+  if (partial && (reinterpret_cast<uintptr_t>(partial) & 15u))
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: partial must be 16-byte aligned");
+
   SuffixParams prm;
-  prm.q = q;
-  prm.q_st = q_stride_token;
-  prm.q_sh = q_stride_head;
-  prm.k = k_local;
-  prm.v = v_local;
-  prm.kv_st = kv_stride_token;
-  prm.kv_sh = kv_stride_head;
-  prm.num_blocks = num_blocks;
-  prm.block_len = block_len;
-  prm.mask_mode = mask_mode;
-  prm.custom_mask = custom_mask;
-  prm.partial = static_cast<const float*>(partial);
   prm.plan = plan;
+  prm.partial = static_cast<const float*>(partial);
   prm.prefix_token = prefix_token;
-  prm.prefix_out = prefix_out;
+  prm.prefix_out = partial ? nullptr : prefix_out;
   prm.po_st = prefix_out_stride_token;
   prm.po_sh = prefix_out_stride_head;
   prm.prefix_lse = prefix_lse;
@@ -344,20 +445,61 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
   prm.lse = lse;
   prm.l_st = lse_stride_token;
   prm.sinks = sinks;
+  prm.custom_mask = custom_mask;
+  prm.status = status;
+  prm.has_local = k_local != nullptr;
+  prm.mask_mode = mask_mode;
   prm.sink_mode = sink_mode;
   prm.Hq = num_qo_heads;
-  prm.Hk = num_kv_heads;
-  prm.G = num_qo_heads / num_kv_heads;
+  prm.G = G;
   prm.scale_log2 = sm_scale * kLog2e;
+
+  CUtensorMap tq, tk, tv;
+  std::memset(&tq, 0, sizeof(tq));
+  std::memset(&tk, 0, sizeof(tk));
+  std::memset(&tv, 0, sizeof(tv));
+  dim3 grid;
+  int NK = 32;
+  if (k_local) {
+    prm.block_len = block_len;
+    NK = block_len <= 32 ? 32 : 64;
+    const CUtensorMapDataType tdt =
+        dtype == D2SD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if (!aligned16(q) || !aligned16(k_local) || !aligned16(v_local) || q_stride_token % 8 ||
+        q_stride_head % 8 || kv_stride_token % 8 || kv_stride_head % 8)
+      return fail(D2SD_ERR_INVALID_ARGUMENT,
+                  "d2sd_suffix_merge: q/k/v must be 16-byte aligned with strides multiple of 8");
+    const uint64_t ntok = static_cast<uint64_t>(num_blocks) * block_len;
+    {
+      const uint64_t dims[3] = {static_cast<uint64_t>(head_dim),
+                                static_cast<uint64_t>(num_qo_heads), ntok};
+      const uint64_t str[2] = {static_cast<uint64_t>(q_stride_head) * 2,
+                               static_cast<uint64_t>(q_stride_token) * 2};
+      const uint32_t box[3] = {64, static_cast<uint32_t>(G), static_cast<uint32_t>(128 / G)};
+      int rc = encode_tensor_map(&tq, tdt, q, 3, dims, str, box, "q");
+      if (rc) return rc;
+    }
+    {
+      const uint64_t dims[3] = {static_cast<uint64_t>(head_dim),
+                                static_cast<uint64_t>(num_kv_heads), ntok};
+      const uint64_t str[2] = {static_cast<uint64_t>(kv_stride_head) * 2,
+                               static_cast<uint64_t>(kv_stride_token) * 2};
+      const uint32_t box[3] = {64, 1, static_cast<uint32_t>(NK)};
+      int rc = encode_tensor_map(&tk, tdt, k_local, 3, dims, str, box, "k_local");
+      if (rc) return rc;
+      rc = encode_tensor_map(&tv, tdt, v_local, 3, dims, str, box, "v_local");
+      if (rc) return rc;
+    }
+    grid = dim3(num_blocks, num_kv_heads, (block_len * G + 127) / 128);
+  } else {
+    // no level 2: the blocks do not matter, tile all tokens of a head together
+    const int64_t ntok = static_cast<int64_t>(num_blocks) * block_len;
+    prm.block_len = static_cast<int32_t>(ntok);
+    grid = dim3(1, num_kv_heads, static_cast<unsigned>((ntok * G + 127) / 128));
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == D2SD_DTYPE_BF16) {
-    return head_dim == 128 ? launch_suffix<__nv_bfloat16, 128>(prm, st)
-                           : launch_suffix<__nv_bfloat16, 64>(prm, st);
-  }
-  if (dtype == D2SD_DTYPE_F16) {
-    return head_dim == 128 ? launch_suffix<__half, 128>(prm, st) : launch_suffix<__half, 64>(prm, st);
-  }
-  return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: dtype must be bf16 or f16");
+  if (dtype == D2SD_DTYPE_BF16) return dispatch_suffix<__nv_bfloat16>(tq, tk, tv, prm, head_dim, NK, grid, st);
+  return dispatch_suffix<__half>(tq, tk, tv, prm, head_dim, NK, grid, st);
 }
 
 extern "C" int d2sd_merge_state(void* v, int64_t v_stride_token, int64_t v_stride_head, float* s,

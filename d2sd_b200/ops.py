@@ -164,11 +164,12 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
                  custom_mask: torch.Tensor | None = None, partial: torch.Tensor | None = None,
                  plan_dev: torch.Tensor | None = None, prefix_token: torch.Tensor | None = None,
                  prefix_out: torch.Tensor | None = None, prefix_lse: torch.Tensor | None = None,
-                 sinks: torch.Tensor | None = None, sink_mode: int = _lib.SINK_NONE) -> None:
+                 sinks: torch.Tensor | None = None, sink_mode: int = _lib.SINK_NONE,
+                 status: torch.Tensor | None = None) -> None:
     """Launch kernel (b). Token-major 3-D views: q/out [tokens, Hq, D],
     k/v_local [tokens, Hk, D], lse/prefix_lse [tokens, Hq]."""
     dev = _require_cuda(q, k_local, v_local, out, lse, custom_mask, partial, plan_dev,
-                        prefix_token, prefix_out, prefix_lse, sinks)
+                        prefix_token, prefix_out, prefix_lse, sinks, status)
     for t in (q, k_local, v_local, out, prefix_out):
         if t is not None and (t.dim() != 3 or t.stride(-1) != 1):
             raise ValueError("token tensors must be [tokens, heads, head_dim], head_dim contiguous")
@@ -191,7 +192,7 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
         prefix_lse.stride(0) if prefix_lse is not None else 0, out.data_ptr(), out.stride(0),
         out.stride(1), _ptr(lse), lse.stride(0) if lse is not None else 0, _ptr(sinks),
         int(sink_mode), int(num_qo_heads), int(num_kv_heads), int(D), dtype_code(out),
-        float(sm_scale), _stream(dev))
+        float(sm_scale), _ptr(status), _stream(dev))
     check(rc, "d2sd_suffix_merge")
 
 

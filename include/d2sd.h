@@ -149,7 +149,11 @@ int d2sd_prefix_attention(const void* q, int64_t q_stride_token,
  * out/lse receive the merged output (q dtype) and base-2 LSE; they may alias
  * prefix_out/prefix_lse. mask_mode is a D2SD_MASK_*, custom_mask is
  * uint64 [num_blocks*block_len] (bit j = token may see block token j).
- * sinks: fp32 [num_qo_heads] or NULL; sink_mode a D2SD_SINK_*. */
+ * sinks: fp32 [num_qo_heads] or NULL; sink_mode a D2SD_SINK_*.
+ * With k_local, q/k_local/v_local must be 16-byte aligned with token and head
+ * strides that are multiples of 8 elements (they are read by TMA), and
+ * block_len <= 64. status (device int32, may be NULL) receives a nonzero code
+ * if a wait inside the kernel ran out of time. */
 int d2sd_suffix_merge(const void* q, int64_t q_stride_token,
                       int64_t q_stride_head, const void* k_local,
                       const void* v_local, int64_t kv_stride_token,
@@ -165,7 +169,7 @@ int d2sd_suffix_merge(const void* q, int64_t q_stride_token,
                       const float* sinks, int32_t sink_mode,
                       int32_t num_qo_heads, int32_t num_kv_heads,
                       int32_t head_dim, int32_t dtype, float sm_scale,
-                      void* stream);
+                      int32_t* status, void* stream);
 
 /* In-place merge of two attention states (v,s) <- merge((v,s),(v_other,s_other))
  * with base-2 LSEs: v [n, heads, head_dim] (dtype), s [n, heads] fp32. */

@@ -132,7 +132,7 @@ def cascade_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
         plan = CascadePlan([Request(n_u, 0, kv_start, kv_len)], Hq, Hk, D, q.device)
     plan.run_prefix(q_pref, k_cache, v_cache, kv_layout, scale, page_table=page_table)
     if out is None:
-        out = torch.empty_like(q)
+        out = torch.empty(B, T, Hq, D, dtype=q.dtype, device=q.device)
     if lse is None:
         lse = torch.empty(B, T, Hq, dtype=torch.float32, device=q.device)
     mode = _MASKS["custom" if custom_mask is not None else ("causal" if causal else "none")]

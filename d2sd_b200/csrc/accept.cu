@@ -15,8 +15,11 @@
 // Ties resolve to the first maximal index and NaN counts as maximal (first NaN
 // wins), the torch.argmax convention.
 //
-// Grid: (chunks, rows). Each CTA reduces one chunk of one row to (value, index)
-// and the last CTA to finish (atomic ticket) reduces the chunks and walks.
+// Work is split into warp items of 2048-element chunks of one logits row (each
+// lane keeps 8 16-byte loads in flight); persistent CTAs walk the items. The
+// warp that finishes a row's last item (per-row atomic count) reduces the row's
+// partials, and the warp that finishes the last row runs the walk, so no
+// single CTA serialises the reduction.
 #include "common.cuh"
 
 namespace d2sd {
@@ -37,40 +40,54 @@ __device__ __forceinline__ bool better(float va, int64_t ia, float vb, int64_t i
   return ia < ib;
 }
 
-__host__ __device__ inline int num_chunks_for(int64_t rows, int64_t vocab, int sms) {
-  // ~8 CTAs per SM over the whole grid, chunks of at least 8192 elements.
-  int64_t target = (static_cast<int64_t>(sms) * 8 + rows - 1) / rows;
-  int64_t max_by_size = (vocab + 8191) / 8192;
-  int64_t c = target < max_by_size ? target : max_by_size;
-  if (c < 1) c = 1;
-  if (c > 64) c = 64;
-  return static_cast<int>(c);
+constexpr int kBatch = 8;       // 16-byte loads in flight per thread
+constexpr int kIdsCache = 2048; // block ids staged in shared memory for the walk
+
+// Stream-K partition of the flattened (row, unit) space over the grid: CTA c
+// owns units [c*W, (c+1)*W), W = ceil(total / grid); a unit is one 16-byte
+// vector (or one element when rows are not 16-byte aligned).
+struct Part {
+  int64_t upr;    // units per row
+  int64_t total;  // rows * upr
+  int64_t W;      // units per CTA
+};
+
+__host__ __device__ inline Part partition(int64_t rows, int64_t upr, int64_t grid) {
+  Part p;
+  p.upr = upr;
+  p.total = rows * upr;
+  p.W = (p.total + grid - 1) / grid;
+  return p;
+}
+
+// Rows a CTA's range can touch: ceil(W / upr) + 1 <= ceil(rows / grid) + 2.
+__host__ __device__ inline int64_t max_segments(int64_t rows, int64_t grid) {
+  return (rows + grid - 1) / grid + 2;
 }
 
 struct Workspace {
-  unsigned int* ticket;  // 1 word, zero between launches
-  float* pval;           // [rows][chunks]
-  int64_t* pidx;         // [rows][chunks]
-  int64_t* amax;         // [rows]
+  unsigned int* ticket;  // CTAs finished; zero between launches
+  float* pval;           // [grid][segs]
+  int64_t* pidx;         // [grid][segs]
+  int64_t segs;
 };
 
 __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
-__host__ __device__ inline int64_t workspace_bytes(int64_t rows, int chunks) {
-  return 256 + align_up(rows * chunks * 4, 256) + align_up(rows * chunks * 8, 256) +
-         align_up(rows * 8, 256);
+__host__ __device__ inline int64_t workspace_bytes(int64_t rows, int64_t grid) {
+  const int64_t n = grid * max_segments(rows, grid);
+  return 256 + align_up(n * 4, 256) + align_up(n * 8, 256);
 }
 
-__host__ __device__ inline Workspace carve(void* base, int64_t rows, int chunks) {
+__host__ __device__ inline Workspace carve(void* base, int64_t rows, int64_t grid) {
   uint8_t* b = static_cast<uint8_t*>(base);
   Workspace w;
+  w.segs = max_segments(rows, grid);
   w.ticket = reinterpret_cast<unsigned int*>(b);
   b += 256;
   w.pval = reinterpret_cast<float*>(b);
-  b += align_up(rows * chunks * 4, 256);
+  b += align_up(grid * w.segs * 4, 256);
   w.pidx = reinterpret_cast<int64_t*>(b);
-  b += align_up(rows * chunks * 8, 256);
-  w.amax = reinterpret_cast<int64_t*>(b);
   return w;
 }
 
@@ -131,139 +148,184 @@ struct VecMax<__half> {
   }
 };
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-    accept_kernel(const T* __restrict__ logits, int B, int TB, int64_t V, int64_t s_b,
-                  int64_t s_t, const int64_t* __restrict__ ids, int64_t ids_sb, int64_t ids_st,
-                  int32_t* result, int64_t* accepted, int64_t* argmax_out, Workspace ws,
-                  int chunks) {
-  constexpr int VN = Vec<T>::N;
-  __shared__ float sv[kThreads / 32];
-  __shared__ int64_t si[kThreads / 32];
-  __shared__ bool last;
-  const int row = blockIdx.y;
-  const int chunk = blockIdx.x;
-  const int b = row / TB, t = row % TB;
-  const T* base = logits + static_cast<int64_t>(b) * s_b + static_cast<int64_t>(t) * s_t;
-  const int64_t csize = ((V + chunks - 1) / chunks + VN - 1) / VN * VN;
-  const int64_t c0 = static_cast<int64_t>(chunk) * csize;
-  const int64_t c1 = c0 + csize < V ? c0 + csize : V;
-
-  // Per-thread scan in increasing index order. Each 16-byte vector is reduced
-  // with a NaN-propagating max first; only a vector that beats the running best
-  // (or holds a NaN) is searched for its first maximal index. A strict ">"
-  // keeps the first index among equal maxima; once the best is NaN nothing
-  // replaces it (torch.argmax: the first NaN wins).
-  float best_v = -INFINITY;
-  int64_t best_i = INT64_MAX;
-  if (c0 < c1) {
-    const bool vec_ok = (reinterpret_cast<uintptr_t>(base + c0) & 15u) == 0;
-    const int64_t nvec = vec_ok ? (c1 - c0) / VN : 0;
-    const int64_t tail0 = c0 + nvec * VN;
-    const uint4* src = reinterpret_cast<const uint4*>(base + c0);
-    if (threadIdx.x < nvec) best_i = c0 + static_cast<int64_t>(threadIdx.x) * VN;
-    auto visit = [&](const uint4& raw, int64_t first) {
-      const float vm = VecMax<T>::max(raw);
-      if (!(vm <= best_v) && best_v == best_v) {
-        const T* e = reinterpret_cast<const T*>(&raw);
+__device__ __forceinline__ void warp_argmax(float& v, int64_t& i) {
 #pragma unroll
-        for (int k = 0; k < VN; ++k) {
-          const float x = Num<T>::to_f(e[k]);
-          if (x != x || x == vm) {
-            best_v = x;
-            best_i = first + k;
-            break;
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better(ov, oi, v, i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+// One thread's scan over units u0, u0+stride, ... < u1 of one row (increasing
+// index order). Each 16-byte vector is reduced with a NaN-propagating max;
+// only a vector that beats the running best (or holds a NaN) is searched for
+// its first maximal index. A strict ">" keeps the first index among equal
+// maxima; once the best is NaN nothing replaces it (first NaN wins).
+template <typename T, bool VEC>
+__device__ __forceinline__ void scan_units(const T* __restrict__ row, int64_t u0, int64_t u1,
+                                           int stride, float& best_v, int64_t& best_i) {
+  constexpr int VN = VEC ? Vec<T>::N : 1;
+  for (int64_t u = u0; u < u1; u += static_cast<int64_t>(stride) * kBatch) {
+    if (VEC) {
+      uint4 raw[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int64_t uu = u + static_cast<int64_t>(k) * stride;
+        if (uu < u1) raw[k] = __ldg(reinterpret_cast<const uint4*>(row) + uu);
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int64_t uu = u + static_cast<int64_t>(k) * stride;
+        if (uu >= u1) break;
+        if (best_i == INT64_MAX) best_i = uu * VN;  // first element seen
+        const float vm = VecMax<T>::max(raw[k]);
+        if (!(vm <= best_v) && best_v == best_v) {
+          const T* e = reinterpret_cast<const T*>(&raw[k]);
+#pragma unroll
+          for (int j = 0; j < Vec<T>::N; ++j) {
+            const float x = Num<T>::to_f(e[j]);
+            if (x != x || x == vm) {
+              best_v = x;
+              best_i = uu * VN + j;
+              break;
+            }
           }
         }
       }
-    };
-    int64_t vI = threadIdx.x;
-    for (; vI + 3 * kThreads < nvec; vI += 4 * kThreads) {
-      uint4 raw[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) raw[u] = __ldg(src + vI + u * kThreads);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) visit(raw[u], c0 + (vI + u * kThreads) * VN);
-    }
-    for (; vI < nvec; vI += kThreads) visit(__ldg(src + vI), c0 + vI * VN);
-    for (int64_t j = tail0 + threadIdx.x; j < c1; j += kThreads) {
-      const float x = Num<T>::to_f(base[j]);
-      if (best_i == INT64_MAX) {
-        best_v = x;
-        best_i = j;
-      } else if ((x > best_v || (x != x)) && best_v == best_v) {
-        best_v = x;
-        best_i = j;
+    } else {
+#pragma unroll 1
+      for (int k = 0; k < kBatch; ++k) {
+        const int64_t uu = u + static_cast<int64_t>(k) * stride;
+        if (uu >= u1) break;
+        const float x = Num<T>::to_f(row[uu]);
+        if (best_i == INT64_MAX) {
+          best_v = x;
+          best_i = uu;
+        } else if ((x > best_v || (x != x)) && best_v == best_v) {
+          best_v = x;
+          best_i = uu;
+        }
       }
     }
   }
-  // block reduce
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-    const int64_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-    if (better(ov, oi, best_v, best_i)) {
-      best_v = ov;
-      best_i = oi;
-    }
-  }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+    accept_kernel(const T* __restrict__ logits, int B, int TB, int64_t V, int64_t s_b,
+                  int64_t s_t, const int64_t* __restrict__ ids, int64_t ids_sb, int64_t ids_st,
+                  int32_t* result, int64_t* accepted, int64_t* argmax_out, Workspace ws, Part pt) {
+  __shared__ float sv[kThreads / 32];
+  __shared__ int64_t si[kThreads / 32];
+  __shared__ bool last;
+  __shared__ int32_t s_amax[64 * 64];
+  __shared__ int64_t s_ids[kIdsCache];
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    sv[warp] = best_v;
-    si[warp] = best_i;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < kThreads / 32; ++w) {
-      if (better(sv[w], si[w], best_v, best_i)) {
-        best_v = sv[w];
-        best_i = si[w];
-      }
+  const int rows = B * TB;
+  const int64_t u_begin = static_cast<int64_t>(blockIdx.x) * pt.W;
+  const int64_t u_end = u_begin + pt.W < pt.total ? u_begin + pt.W : pt.total;
+  int seg = 0;
+  for (int64_t u = u_begin; u < u_end; ++seg) {
+    const int64_t r = u / pt.upr;
+    const int64_t re = (r + 1) * pt.upr < u_end ? (r + 1) * pt.upr : u_end;
+    const int b = static_cast<int>(r / TB), t = static_cast<int>(r % TB);
+    const T* base = logits + static_cast<int64_t>(b) * s_b + static_cast<int64_t>(t) * s_t;
+    float bv = -INFINITY;
+    int64_t bi = INT64_MAX;
+    scan_units<T, VEC>(base, u - r * pt.upr + threadIdx.x, re - r * pt.upr, kThreads, bv, bi);
+    warp_argmax(bv, bi);
+    if (lane == 0) {
+      sv[warp] = bv;
+      si[warp] = bi;
     }
-    ws.pval[static_cast<int64_t>(row) * chunks + chunk] = best_v;
-    ws.pidx[static_cast<int64_t>(row) * chunks + chunk] = best_i;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < kThreads / 32; ++w) {
+        if (better(sv[w], si[w], bv, bi)) {
+          bv = sv[w];
+          bi = si[w];
+        }
+      }
+      ws.pval[blockIdx.x * ws.segs + seg] = bv;
+      ws.pidx[blockIdx.x * ws.segs + seg] = bi;
+    }
+    __syncthreads();
+    u = re;
+  }
+  if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned total = gridDim.x * gridDim.y;
-    last = atomicAdd(ws.ticket, 1u) == total - 1;
+    last = atomicAdd(ws.ticket, 1u) == gridDim.x - 1;
   }
   __syncthreads();
   if (!last) return;
   __threadfence();
 
-  // ---- last CTA: per-row argmax over chunks ----
-  const int rows = B * TB;
+  // ---- last CTA: stage the block ids, then per-row argmax over the (at most
+  // a few) CTA segments of the row ----
+  const bool ids_cached = rows <= kIdsCache;
+  if (ids_cached) {
+    for (int r = threadIdx.x; r < rows; r += kThreads)
+      s_ids[r] = ids[(r / TB) * ids_sb + (r % TB) * ids_st];
+  }
   for (int r = threadIdx.x; r < rows; r += kThreads) {
-    float bv = -INFINITY;
-    int64_t bi = INT64_MAX;
-    for (int c = 0; c < chunks; ++c) {
-      const float v = ws.pval[static_cast<int64_t>(r) * chunks + c];
-      const int64_t ix = ws.pidx[static_cast<int64_t>(r) * chunks + c];
-      if (better(v, ix, bv, bi)) {
-        bv = v;
-        bi = ix;
+    const int64_t c_first = (static_cast<int64_t>(r) * pt.upr) / pt.W;
+    const int64_t c_last = ((static_cast<int64_t>(r) + 1) * pt.upr - 1) / pt.W;
+    float v[4];
+    int64_t ix[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {  // the common case: up to 4 segments, loads in flight together
+      const int64_t c = c_first + k;
+      if (c <= c_last) {
+        const int64_t seg = r - (c * pt.W) / pt.upr;  // segment of CTA c holding row r
+        v[k] = __ldcg(ws.pval + c * ws.segs + seg);
+        ix[k] = __ldcg(ws.pidx + c * ws.segs + seg);
       }
     }
-    if (bi == INT64_MAX) bi = 0;  // row of only -inf: torch returns 0
-    ws.amax[r] = bi;
+    float bv = -INFINITY;
+    int64_t bi = INT64_MAX;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (c_first + k <= c_last && better(v[k], ix[k], bv, bi)) {
+        bv = v[k];
+        bi = ix[k];
+      }
+    }
+    for (int64_t c = c_first + 4; c <= c_last; ++c) {
+      const int64_t seg = r - (c * pt.W) / pt.upr;
+      const float vv = __ldcg(ws.pval + c * ws.segs + seg);
+      const int64_t ii = __ldcg(ws.pidx + c * ws.segs + seg);
+      if (better(vv, ii, bv, bi)) {
+        bv = vv;
+        bi = ii;
+      }
+    }
+    if (bi == INT64_MAX) bi = 0;
+    s_amax[r] = static_cast<int32_t>(bi);
     if (argmax_out) argmax_out[r] = bi;
   }
   __syncthreads();
 
-  // ---- the acceptance walk on warp 0 ----
+  // ---- the acceptance walk on warp 0 (valid set as a 64-bit mask) ----
   if (warp == 0) {
-    // valid set as a 64-bit mask; lane l owns branches l and l + 32
     uint64_t valid = (B >= 64) ? ~0ull : ((1ull << B) - 1ull);
     int acc = 0;
     int vb = 0;
     while (true) {
       vb = __ffsll(static_cast<long long>(valid)) - 1;
-      const int64_t tok = ws.amax[vb * TB + acc];
+      const int64_t tok = s_amax[vb * TB + acc];
       if (lane == 0) accepted[acc] = tok;
       acc += 1;
       if (acc == TB) break;
       bool m0 = false, m1 = false;
-      if (lane < B) m0 = ids[lane * ids_sb + acc * ids_st] == tok;
-      if (lane + 32 < B) m1 = ids[(lane + 32) * ids_sb + acc * ids_st] == tok;
+      if (lane < B)
+        m0 = (ids_cached ? s_ids[lane * TB + acc] : ids[lane * ids_sb + acc * ids_st]) == tok;
+      if (lane + 32 < B)
+        m1 = (ids_cached ? s_ids[(lane + 32) * TB + acc]
+                         : ids[(lane + 32) * ids_sb + acc * ids_st]) == tok;
       const uint64_t match = static_cast<uint64_t>(__ballot_sync(0xffffffffu, m0)) |
                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, m1)) << 32);
       valid &= match;
@@ -273,7 +335,7 @@ __global__ void __launch_bounds__(kThreads)
     if (lane == 0) {
       result[0] = acc;
       result[1] = vb;
-      *ws.ticket = 0u;  // leave the workspace ready for the next launch
+      *ws.ticket = 0u;  // leave the workspace zeroed for the next launch
     }
   }
 }
@@ -281,12 +343,43 @@ __global__ void __launch_bounds__(kThreads)
 }  // namespace
 }  // namespace d2sd
 
+namespace d2sd {
+namespace {
+int accept_grid() { return current_sm_count() * 3; }
+
+template <typename T>
+int launch_accept(const void* logits, int B, int TB, int64_t V, int64_t sb, int64_t st,
+                  const int64_t* ids, int64_t isb, int64_t ist, int32_t* result, int64_t* acc_ids,
+                  int64_t* argmax_out, void* workspace, int64_t wbytes, cudaStream_t stream) {
+  constexpr int VN = Vec<T>::N;
+  const int64_t rows = static_cast<int64_t>(B) * TB;
+  const int grid = accept_grid();
+  if (rows > 64 * 64)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: at most 4096 logits rows");
+  if (wbytes < workspace_bytes(rows, grid))
+    return fail(D2SD_ERR_WORKSPACE, "d2sd_verify_accept: workspace too small");
+  Workspace ws = carve(workspace, rows, grid);
+  const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && V % VN == 0 &&
+                   sb % VN == 0 && st % VN == 0;
+  const int64_t upr = vec ? V / VN : V;
+  Part pt = partition(rows, upr, grid);
+  if (vec)
+    accept_kernel<T, true><<<grid, kThreads, 0, stream>>>(
+        static_cast<const T*>(logits), B, TB, V, sb, st, ids, isb, ist, result, acc_ids,
+        argmax_out, ws, pt);
+  else
+    accept_kernel<T, false><<<grid, kThreads, 0, stream>>>(
+        static_cast<const T*>(logits), B, TB, V, sb, st, ids, isb, ist, result, acc_ids,
+        argmax_out, ws, pt);
+  return check_launch("accept_kernel");
+}
+}  // namespace
+}  // namespace d2sd
+
 extern "C" int64_t d2sd_verify_accept_workspace_size(int32_t num_branches, int32_t block_len,
                                                      int64_t vocab) {
   if (num_branches <= 0 || block_len <= 0 || vocab <= 0) return -1;
-  const int64_t rows = static_cast<int64_t>(num_branches) * block_len;
-  const int chunks = d2sd::num_chunks_for(rows, vocab, d2sd::current_sm_count());
-  return d2sd::workspace_bytes(rows, chunks);
+  return d2sd::workspace_bytes(static_cast<int64_t>(num_branches) * block_len, d2sd::accept_grid());
 }
 
 extern "C" int d2sd_verify_accept(const void* logits, int32_t dtype, int32_t num_branches,
@@ -301,38 +394,25 @@ extern "C" int d2sd_verify_accept(const void* logits, int32_t dtype, int32_t num
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_verify_accept: invalid argument");
   if (num_branches > kMaxBranches)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: at most 64 branches");
-  const int64_t rows = static_cast<int64_t>(num_branches) * block_len;
-  if (rows > 65535)
-    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: too many logits rows");
-  const int chunks = num_chunks_for(rows, vocab, current_sm_count());
-  if (workspace_bytes < d2sd::workspace_bytes(rows, chunks))
-    return fail(D2SD_ERR_WORKSPACE, "d2sd_verify_accept: workspace too small");
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_verify_accept: workspace must be 256-byte aligned");
-  Workspace ws = carve(workspace, rows, chunks);
-  dim3 grid(chunks, static_cast<unsigned>(rows));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case D2SD_DTYPE_F32:
-      accept_kernel<float><<<grid, kThreads, 0, st>>>(
-          static_cast<const float*>(logits), num_branches, block_len, vocab, stride_branch,
-          stride_pos, block_ids, ids_stride_branch, ids_stride_pos, result, accepted_ids,
-          argmax_out, ws, chunks);
-      break;
+      return launch_accept<float>(logits, num_branches, block_len, vocab, stride_branch,
+                                  stride_pos, block_ids, ids_stride_branch, ids_stride_pos,
+                                  result, accepted_ids, argmax_out, workspace, workspace_bytes, st);
     case D2SD_DTYPE_BF16:
-      accept_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(
-          static_cast<const __nv_bfloat16*>(logits), num_branches, block_len, vocab,
-          stride_branch, stride_pos, block_ids, ids_stride_branch, ids_stride_pos, result,
-          accepted_ids, argmax_out, ws, chunks);
-      break;
+      return launch_accept<__nv_bfloat16>(logits, num_branches, block_len, vocab, stride_branch,
+                                          stride_pos, block_ids, ids_stride_branch,
+                                          ids_stride_pos, result, accepted_ids, argmax_out,
+                                          workspace, workspace_bytes, st);
     case D2SD_DTYPE_F16:
-      accept_kernel<__half><<<grid, kThreads, 0, st>>>(
-          static_cast<const __half*>(logits), num_branches, block_len, vocab, stride_branch,
-          stride_pos, block_ids, ids_stride_branch, ids_stride_pos, result, accepted_ids,
-          argmax_out, ws, chunks);
-      break;
+      return launch_accept<__half>(logits, num_branches, block_len, vocab, stride_branch,
+                                   stride_pos, block_ids, ids_stride_branch, ids_stride_pos,
+                                   result, accepted_ids, argmax_out, workspace, workspace_bytes,
+                                   st);
     default:
       return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: unknown dtype");
   }
-  return check_launch("accept_kernel");
 }

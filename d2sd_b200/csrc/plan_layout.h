@@ -16,6 +16,12 @@
 
 #include <stdint.h>
 
+#ifdef __CUDACC__
+#define D2SD_HOST_DEVICE __host__ __device__
+#else
+#define D2SD_HOST_DEVICE
+#endif
+
 namespace d2sd {
 namespace plan {
 
@@ -54,6 +60,12 @@ constexpr int I_KV_END = 7;     // one past the last visible key position
 constexpr int I_SLOT0 = 8;      // partial slot of query tile 0
 constexpr int I_SLOT1 = 9;      // partial slot of query tile 1 (-1 if none)
 constexpr int I_QTOK = 10;      // Q-tensor token index of query tile 0's row 0
+
+// Partial-state slot (one per item per query tile): the normalised O of its
+// 128 rows in bf16 ([128][head_dim], row-major), then their base-2 LSEs in fp32.
+D2SD_HOST_DEVICE constexpr int64_t slot_bytes(int head_dim) {
+  return static_cast<int64_t>(kTileRows) * head_dim * 2 + kTileRows * 4;
+}
 
 // unit: (slot_base, num_slots)
 constexpr int kUnitInts = 2;

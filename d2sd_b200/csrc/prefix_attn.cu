@@ -57,14 +57,13 @@ struct Cfg {
   static constexpr int B_OFREE = B_OFINAL + 2;
   static constexpr int kNumBars = B_OFREE + 2;
   static constexpr int kSmemBytes = kSmemBar + kNumBars * 8 + 16 + 1024;  // + align slack
-  static constexpr int kSlotFloats = kTileRows * (D + 1);
 };
 
 struct PrefixParams {
   const int32_t* plan;
   const int32_t* page_table;         // nullptr: contiguous KV
   const int32_t* page_table_offset;  // per request
-  float* partial;
+  void* partial;
   int32_t* status;
   int32_t rows_per_box;  // page_size (paged) or 16 (contiguous)
   int32_t G;
@@ -88,78 +87,89 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return ok != 0;
 }
 
+// Producer warp. Lane 0 issues every TMA; the page indices of a KV tile are
+// fetched by the whole warp (lane b reads page b of the tile) one tile ahead
+// of their use, so no TMA waits on a dependent page-table load.
 template <int D>
 __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                          const PrefixParams& p, uint8_t* smem, uint64_t* bars, volatile int* abort,
                          int item_begin, int item_end) {
   using C = Cfg<D>;
+  const int lane = threadIdx.x & 31;
   const int32_t* items = p.plan + p.plan[H_OFF_ITEMS];
   const int G = p.G;
   const int rpb = p.rows_per_box;
-  const int boxes = kTileKeys / rpb;
+  const int boxes = kTileKeys / rpb;  // <= 16
   uint32_t kt = 0;
-  for (int it = item_begin; it < item_end; ++it) {
+  bool alive = true;
+  for (int it = item_begin; it < item_end && alive; ++it) {
     const int32_t* I = items + it * kItemInts;
     const int r = I[I_REQ], h = I[I_HEAD], t0 = I[I_T0], t1 = I[I_T1];
     const int kv_end = I[I_KV_END], qtok = I[I_QTOK];
-    if (it > item_begin) {
-      if (!mbar_wait(&bars[C::B_QFREE], (it - item_begin - 1) & 1, abort)) return;
-    }
-    mbar_arrive_expect_tx(&bars[C::B_QFULL], 2 * C::kTileBytes);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-#pragma unroll
-      for (int pn = 0; pn < C::kPanels; ++pn) {
-        tma_load_3d(smem + C::kSmemQ + i * C::kTileBytes + pn * kPanelBytes, tm_q,
-                    &bars[C::B_QFULL], pn * 64, h * G, qtok + i * (kTileRows / G));
-      }
-    }
     const int base = p.page_table_offset ? p.page_table_offset[r] : 0;
     const int last_page = (kv_end - 1) / rpb;
-    for (int t = t0; t < t1; ++t, ++kt) {
+    // lane b: coordinate of box b of a tile (page index, or first token)
+    auto box_coord = [&](int t) -> int {
+      const int pos0 = t * kTileKeys + lane * rpb;
+      if (p.page_table) {
+        int pg = pos0 / rpb;
+        if (pg > last_page) pg = last_page;  // finite filler, masked in softmax
+        return lane < boxes ? p.page_table[base + pg] : 0;
+      }
+      return base + pos0;
+    };
+    int coord = box_coord(t0);
+    if (lane == 0) {
+      if (it > item_begin && !mbar_wait(&bars[C::B_QFREE], (it - item_begin - 1) & 1, abort))
+        alive = false;
+      if (alive) {
+        mbar_arrive_expect_tx(&bars[C::B_QFULL], 2 * C::kTileBytes);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+#pragma unroll
+          for (int pn = 0; pn < C::kPanels; ++pn) {
+            tma_load_3d(smem + C::kSmemQ + i * C::kTileBytes + pn * kPanelBytes, tm_q,
+                        &bars[C::B_QFULL], pn * 64, h * G, qtok + i * (kTileRows / G));
+          }
+        }
+      }
+    }
+    alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
+    for (int t = t0; t < t1 && alive; ++t, ++kt) {
+      const int next = (t + 1 < t1) ? box_coord(t + 1) : 0;  // prefetch the next tile's pages
       const int s = static_cast<int>(kt % C::kStages);
       const uint32_t use = kt / C::kStages;
-      if (use > 0) {
-        if (!mbar_wait(&bars[C::B_KVEMPTY + s], (use - 1) & 1, abort)) return;
-      }
+      if (lane == 0 && use > 0 && !mbar_wait(&bars[C::B_KVEMPTY + s], (use - 1) & 1, abort))
+        alive = false;
+      alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
+      if (!alive) break;
       uint8_t* ks = smem + C::kSmemK + s * C::kTileBytes;
       uint8_t* vs = smem + C::kSmemV + s * C::kTileBytes;
-      mbar_arrive_expect_tx(&bars[C::B_KFULL + s], C::kTileBytes);
+      if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_KFULL + s], C::kTileBytes);
       for (int b = 0; b < boxes; ++b) {
-        const int pos0 = t * kTileKeys + b * rpb;
-        int c1, c3;
-        if (p.page_table) {
-          int pg = pos0 / rpb;
-          if (pg > last_page) pg = last_page;  // finite filler, masked in softmax
-          c1 = 0;
-          c3 = p.page_table[base + pg];
-        } else {
-          c1 = base + pos0;
-          c3 = 0;
-        }
+        const int cb = __shfl_sync(0xffffffffu, coord, b);
+        const int c1 = p.page_table ? 0 : cb;
+        const int c3 = p.page_table ? cb : 0;
+        if (lane == 0) {
 #pragma unroll
-        for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_load_4d(ks + pn * kPanelBytes + b * rpb * 128, tm_k, &bars[C::B_KFULL + s], pn * 64,
-                      c1, h, c3);
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_4d(ks + pn * kPanelBytes + b * rpb * 128, tm_k, &bars[C::B_KFULL + s],
+                        pn * 64, c1, h, c3);
+        }
       }
-      mbar_arrive_expect_tx(&bars[C::B_VFULL + s], C::kTileBytes);
+      if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_VFULL + s], C::kTileBytes);
       for (int b = 0; b < boxes; ++b) {
-        const int pos0 = t * kTileKeys + b * rpb;
-        int c1, c3;
-        if (p.page_table) {
-          int pg = pos0 / rpb;
-          if (pg > last_page) pg = last_page;
-          c1 = 0;
-          c3 = p.page_table[base + pg];
-        } else {
-          c1 = base + pos0;
-          c3 = 0;
-        }
+        const int cb = __shfl_sync(0xffffffffu, coord, b);
+        const int c1 = p.page_table ? 0 : cb;
+        const int c3 = p.page_table ? cb : 0;
+        if (lane == 0) {
 #pragma unroll
-        for (int pn = 0; pn < C::kPanels; ++pn)
-          tma_load_4d(vs + pn * kPanelBytes + b * rpb * 128, tm_v, &bars[C::B_VFULL + s], pn * 64,
-                      c1, h, c3);
+          for (int pn = 0; pn < C::kPanels; ++pn)
+            tma_load_4d(vs + pn * kPanelBytes + b * rpb * 128, tm_v, &bars[C::B_VFULL + s],
+                        pn * 64, c1, h, c3);
+        }
       }
+      coord = next;
     }
   }
 }
@@ -352,23 +362,27 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
     if (!warp_wait(&bars[C::B_OFINAL + i], k & 1, abort)) return;
     tc_fence_after();
     if (slot >= 0) {
+      // normalised O of this row in bf16 (the precision FlashInfer hands to its
+      // merge), base-2 LSE in fp32
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      float* dst = p.partial + static_cast<int64_t>(slot) * C::kSlotFloats +
-                   static_cast<int64_t>(row) * D;
+      uint8_t* sb = reinterpret_cast<uint8_t*>(p.partial) + static_cast<int64_t>(slot) * slot_bytes(D);
+      uint4* dst = reinterpret_cast<uint4*>(sb + static_cast<int64_t>(row) * D * 2);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld32_wait(lane_base + o_col(i) + c * 32, o);
-        float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          d4[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
-                              __uint_as_float(o[4 * e + 2]) * inv,
-                              __uint_as_float(o[4 * e + 3]) * inv);
+        for (int e = 0; e < 4; ++e) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv);
+          v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv);
+          v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv);
+          v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv);
+          dst[c * 4 + e] = v;
         }
       }
       const float lse = l_run > 0.f ? m_run + fast_log2(l_run) : -INFINITY;
-      p.partial[static_cast<int64_t>(slot) * C::kSlotFloats + kTileRows * D + row] = lse;
+      reinterpret_cast<float*>(sb + static_cast<int64_t>(kTileRows) * D * 2)[row] = lse;
     }
     tc_fence_before();
     __syncwarp();
@@ -377,7 +391,7 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
 }
 
 template <int D>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kNumThreads, 1)
     prefix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v, const PrefixParams p) {
@@ -427,7 +441,7 @@ __global__ void __maxnreg__(200)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kTmaWarp) {
-    if (lane == 0) producer<D>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
+    producer<D>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
     __syncwarp();
   } else if (warp == kMmaWarp) {
     if (lane == 0) mma_issuer<D>(p, smem, bars, tmem, abort, item_begin, item_end);
@@ -471,7 +485,7 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
 }  // namespace d2sd
 
 extern "C" int64_t d2sd_partial_slot_bytes(int32_t head_dim) {
-  return static_cast<int64_t>(d2sd::plan::kTileRows) * (head_dim + 1) * 4;
+  return d2sd::plan::slot_bytes(head_dim);
 }
 
 extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int64_t q_stride_head,
@@ -553,7 +567,7 @@ extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int6
   prm.plan = plan;
   prm.page_table = page_table;
   prm.page_table_offset = page_table_offset;
-  prm.partial = static_cast<float*>(partial);
+  prm.partial = partial;
   prm.status = status;
   prm.rows_per_box = rows_per_box;
   prm.G = G;

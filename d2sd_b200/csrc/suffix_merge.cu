@@ -28,13 +28,13 @@ namespace {
 
 using namespace plan;
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 512;
 constexpr int kMaxBlockLen = 64;
 constexpr int kPanelQ = 128 * 128;  // 128 rows x 128 bytes
 
 struct SuffixParams {
   const int32_t* plan;
-  const float* partial;
+  const void* partial;
   const int32_t* prefix_token;
   const void* prefix_out;
   int64_t po_st, po_sh;
@@ -63,7 +63,10 @@ struct SCfg {
   static constexpr int kSmemK = kQBytes;
   static constexpr int kSmemV = kSmemK + kKVBytes;
   static constexpr int kSmemBar = kSmemV + kKVBytes;
-  static constexpr int kSmemBytes = kSmemBar + 64 + 1024;
+  static constexpr int kSmemMeta = kSmemBar + 64;
+  static constexpr int kSmemBytes = kSmemMeta + 64 * 32 + 1024;
+  // the staged local output [64][D + 4] fp32 reuses the Q/K/V region
+  static_assert(64 * (D + 4) * 4 <= kSmemBar, "stage does not fit");
 };
 
 template <typename T>
@@ -93,32 +96,48 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return ok != 0;
 }
 
+// Per merge row, written by phase 1, read by phase 2.
+struct RowMeta {
+  float lse_local;   // base-2 LSE of the level-2 (local) part, -inf if none
+  int32_t tok;       // token index, -1 if the row is padding
+  int32_t hq;        // query head
+  int32_t slot;      // first partial slot of the row's query tile (partial mode)
+  int32_t nslots;    // number of partial slots (partial mode)
+  int32_t prow;      // row inside the slot
+  int32_t pad[2];
+};
+
 template <typename T, int D, int NK>
 __global__ void __launch_bounds__(kThreads)
     suffix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v, const SuffixParams p) {
   using C = SCfg<D, NK>;
+  constexpr int SP = D + 4;  // padded fp32 row of the staged local output
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSmemBar);  // load, S, O
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  RowMeta* meta = reinterpret_cast<RowMeta*>(smem + C::kSmemMeta);
+  float* stage = reinterpret_cast<float*>(smem + C::kSmemQ);  // reuses Q after the MMAs
 
-  const int blk = blockIdx.x, h = blockIdx.y, rt = blockIdx.z;
+  const int blk = blockIdx.x, h = blockIdx.y;
+  const int rt = blockIdx.z >> 1, half = blockIdx.z & 1;  // 128-row tile, 64-row merge half
   const int TB = p.block_len, G = p.G;
-  const int warp = threadIdx.x / 32;
-  const int R = rt * 128 + threadIdx.x;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const float sl2 = p.scale_log2;
+
+  // ---- phase 1a: level-2 attention on tcgen05 (warps 0-3, thread = row) ----
+  uint32_t tmem = 0;
+  bool ok = true;
+  float lse_l = -INFINITY, inv_l = 0.f;
+  const int row = threadIdx.x & 127;  // TMEM lane of warps 0-3
+  const int R = rt * 128 + row;
   const int t = R / G, g = R - (R / G) * G;
   const bool valid = t < TB;
   const int tok = blk * TB + t;
-  const int hq = h * G + g;
-  const float sl2 = p.scale_log2;
-
-  float lse_l = -INFINITY, inv_l = 0.f;
-  uint32_t tmem = 0;
-  bool ok = true;
   if (p.has_local) {
     if (threadIdx.x == 0) {
       for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
@@ -134,7 +153,6 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
     tc_fence_after();
     tmem = *tmem_slot;
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(&bars[0], C::kQBytes + 2 * C::kKVBytes);
 #pragma unroll
@@ -159,47 +177,52 @@ __global__ void __launch_bounds__(kThreads)
         umma_commit(&bars[1]);
       }
     }
-    ok = warp_wait(&bars[1], 0, abort);
-    float l = 0.f, m = -INFINITY;
-    if (ok) {
-      tc_fence_after();
-      uint32_t s[NK];
-      tmem_ld32_wait(lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      if (NK == 64) tmem_ld32_wait(lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 % NK]));
-      uint64_t allowed = 0;
-      if (valid) {
-        if (p.mask_mode == D2SD_MASK_CAUSAL) allowed = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
-        else if (p.mask_mode == D2SD_MASK_CUSTOM) allowed = p.custom_mask[tok];
-        else allowed = ~0ull;
-        if (TB < 64) allowed &= (1ull << TB) - 1ull;
-      }
-#pragma unroll
-      for (int j = 0; j < NK; ++j) {
-        if (!((allowed >> j) & 1ull)) s[j] = 0xff800000u;
-        m = fmaxf(m, __uint_as_float(s[j]));
-      }
-      const float mm = (m == -INFINITY) ? 0.f : m * sl2;
-#pragma unroll
-      for (int c = 0; c < NK / 32; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, -mm));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, -mm));
-          l += p0 + p1;
-          pk[e] = Fmt<T>::pack(p0, p1);
+    if (warp < 4) {
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      ok = warp_wait(&bars[1], 0, abort);
+      if (ok) {
+        tc_fence_after();
+        uint32_t s[NK];
+        tmem_ld32_wait(lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+        if (NK == 64)
+          tmem_ld32_wait(lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 % NK]));
+        uint64_t allowed = 0;
+        if (valid) {
+          if (p.mask_mode == D2SD_MASK_CAUSAL) allowed = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
+          else if (p.mask_mode == D2SD_MASK_CUSTOM) allowed = p.custom_mask[tok];
+          else allowed = ~0ull;
+          if (TB < 64) allowed &= (1ull << TB) - 1ull;
         }
-        tmem_st16(lane_base + c * 16, pk);
-      }
-      tmem_st_wait();
-      if (l > 0.f) {
-        lse_l = mm + fast_log2(l);
-        inv_l = 1.f / l;
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < NK; ++j) {
+          if (!((allowed >> j) & 1ull)) s[j] = 0xff800000u;
+          m = fmaxf(m, __uint_as_float(s[j]));
+        }
+        const float mm = (m == -INFINITY) ? 0.f : m * sl2;
+        float l = 0.f;
+#pragma unroll
+        for (int c = 0; c < NK / 32; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, -mm));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, -mm));
+            l += p0 + p1;
+            pk[e] = Fmt<T>::pack(p0, p1);
+          }
+          tmem_st16(lane_base + c * 16, pk);
+        }
+        tmem_st_wait();
+        if (l > 0.f) {
+          lse_l = mm + fast_log2(l);
+          inv_l = 1.f / l;
+        }
       }
     }
     tc_fence_before();
     __syncthreads();
-    if (threadIdx.x == 0 && ok && !*abort) {
+    if (threadIdx.x == 0 && !*abort) {
       tc_fence_after();
       constexpr uint32_t idesc = umma_idesc(128, D, true, Fmt<T>::kUmma);
       const uint32_t b0 = smem_u32(smem + C::kSmemV);
@@ -210,110 +233,162 @@ __global__ void __launch_bounds__(kThreads)
       }
       umma_commit(&bars[2]);
     }
-    ok = ok && warp_wait(&bars[2], 0, abort);
-    tc_fence_after();
-  }
-
-  // ---- prefix states: their LSEs first (max and denominator) ----
-  int slot_base = 0, nslots = 0;
-  const T* po = nullptr;
-  float lse_p = -INFINITY;
-  if (valid && p.partial) {
-    const int32_t* pl = p.plan;
-    const int ptok = p.prefix_token ? p.prefix_token[tok] : tok;
-    const int req = (ptok >= 0 && ptok < pl[H_NUM_TOKENS]) ? pl[pl[H_OFF_TOKENS] + ptok] : -1;
-    if (req >= 0) {
-      const int32_t* rq = pl + pl[H_OFF_REQUESTS] + req * kReqInts;
-      const int qrow = (ptok - rq[2]) * G + g;
-      const int32_t* un = pl + pl[H_OFF_UNITS] + (rq[0] + h * rq[1] + qrow / kTileRows) * kUnitInts;
-      slot_base = un[0] * kTileRows + (qrow % kTileRows);  // row index into the slot array
-      nslots = un[1];
+    if (warp < 4) {
+      ok = warp_wait(&bars[2], 0, abort) && ok;
+      tc_fence_after();
     }
-  } else if (valid && p.prefix_out) {
-    po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(tok) * p.po_st +
-         static_cast<int64_t>(hq) * p.po_sh;
-    lse_p = p.prefix_lse[static_cast<int64_t>(tok) * p.pl_st + hq];
   }
-  const int64_t slot_floats = static_cast<int64_t>(kTileRows) * (D + 1);
-  // slot_base = slot*128 + prow; the row's O starts at slot*slot_floats + prow*D
-  auto slot_row = [&](int s) -> int64_t {
-    const int64_t idx = slot_base + static_cast<int64_t>(s) * kTileRows;
-    return (idx / kTileRows) * slot_floats + (idx % kTileRows) * D;
-  };
-  auto slot_lse = [&](int s) -> float {
-    const int64_t idx = slot_base + static_cast<int64_t>(s) * kTileRows;
-    return p.partial[(idx / kTileRows) * slot_floats + kTileRows * D + (idx % kTileRows)];
-  };
-  float M = lse_l;
-  for (int s = 0; s < nslots; ++s) M = fmaxf(M, slot_lse(s));
-  M = fmaxf(M, lse_p);
-  const float Mz = (M == -INFINITY) ? 0.f : M;
-  const float w_l = (lse_l == -INFINITY) ? 0.f : fast_exp2(lse_l - Mz);
-  const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
-  float den = w_l + w_p;
-  for (int s = 0; s < nslots; ++s) {
-    const float ls = slot_lse(s);
-    den += (ls == -INFINITY) ? 0.f : fast_exp2(ls - Mz);
-  }
-  const float lse_out = den > 0.f ? Mz + fast_log2(den) : -INFINITY;
-  float factor = den > 0.f ? 1.f / den : 0.f;
-  if (p.sinks && p.sink_mode != D2SD_SINK_NONE && valid) {
-    const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse_out * kLn2 : lse_out) - p.sinks[hq];
-    factor *= 1.f / (1.f + __expf(-x));
-  }
-  const float wl = w_l * inv_l;  // local O is unnormalised in TMEM
 
-  // ---- epilogue, 32 columns at a time ----
-  T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(tok) * p.o_st +
-            static_cast<int64_t>(hq) * p.o_sh;
-#pragma unroll 1
-  for (int c = 0; c < D / 32; ++c) {
-    float o[32];
+  // ---- phase 1b: rows of this CTA's merge half: local O -> smem, metadata ----
+  if (warp / 2 == half) {  // warps 2*half, 2*half+1 own TMEM lanes [64*half, 64*half+64)
+    const int lr = row - 64 * half;
+    RowMeta mt;
+    mt.lse_local = (p.has_local && ok) ? lse_l : -INFINITY;
+    mt.tok = valid ? tok : -1;
+    mt.hq = h * G + g;
+    mt.slot = 0;
+    mt.nslots = 0;
+    mt.prow = 0;
+    if (valid && p.partial) {
+      const int32_t* pl = p.plan;
+      const int ptok = p.prefix_token ? p.prefix_token[tok] : tok;
+      const int req = (ptok >= 0 && ptok < pl[H_NUM_TOKENS]) ? pl[pl[H_OFF_TOKENS] + ptok] : -1;
+      if (req >= 0) {
+        const int32_t* rq = pl + pl[H_OFF_REQUESTS] + req * kReqInts;
+        const int qrow = (ptok - rq[2]) * G + g;
+        const int32_t* un =
+            pl + pl[H_OFF_UNITS] + (rq[0] + h * rq[1] + qrow / kTileRows) * kUnitInts;
+        mt.slot = un[0];
+        mt.nslots = un[1];
+        mt.prow = qrow % kTileRows;
+      }
+    }
+    meta[lr] = mt;
     if (p.has_local) {
-      uint32_t r[32];
-      tmem_ld32_wait(tmem + (static_cast<uint32_t>(warp * 32) << 16) + 128 + c * 32, r);
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      const float sc = ok ? inv_l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32_wait(lane_base + 128 + c * 32, o);
+        float4* dst = reinterpret_cast<float4*>(stage + lr * SP + c * 32);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) o[e] = ok ? __uint_as_float(r[e]) * wl : 0.f;
+        for (int e = 0; e < 8; ++e)
+          dst[e] = make_float4(__uint_as_float(o[4 * e]) * sc, __uint_as_float(o[4 * e + 1]) * sc,
+                               __uint_as_float(o[4 * e + 2]) * sc,
+                               __uint_as_float(o[4 * e + 3]) * sc);
+      }
+    }
+  }
+  if (p.has_local) tc_fence_before();
+  __syncthreads();
+  if (p.has_local && warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+  if (p.has_local && threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
+
+  // ---- phase 2: merge rows, one warp per row, lanes across columns ----
+  constexpr int CPL = D / 32;  // columns per lane
+  const int64_t sbytes = slot_bytes(D);
+  const uint8_t* part = static_cast<const uint8_t*>(p.partial);
+  for (int lr = warp; lr < 64; lr += kThreads / 32) {
+    const RowMeta mt = meta[lr];
+    if (mt.tok < 0) continue;
+    // the row's states: local, dense prefix, or partial slots
+    float lse_p = -INFINITY;
+    const T* po = nullptr;
+    if (!p.partial && p.prefix_out) {
+      po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(mt.tok) * p.po_st +
+           static_cast<int64_t>(mt.hq) * p.po_sh;
+      lse_p = p.prefix_lse[static_cast<int64_t>(mt.tok) * p.pl_st + mt.hq];
+    }
+    float M = fmaxf(mt.lse_local, lse_p);
+    for (int s0 = 0; s0 < mt.nslots; s0 += 32) {
+      float ls = -INFINITY;
+      if (s0 + lane < mt.nslots)
+        ls = *reinterpret_cast<const float*>(part + (mt.slot + s0 + lane) * sbytes +
+                                             kTileRows * D * 2 + mt.prow * 4);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ls = fmaxf(ls, __shfl_xor_sync(0xffffffffu, ls, o));
+      M = fmaxf(M, ls);
+    }
+    const float Mz = (M == -INFINITY) ? 0.f : M;
+    const float w_l = (mt.lse_local == -INFINITY) ? 0.f : fast_exp2(mt.lse_local - Mz);
+    const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
+    float acc[CPL];
+    if (p.has_local) {
+      const float* st = stage + lr * SP + lane * CPL;
+#pragma unroll
+      for (int e = 0; e < CPL; ++e) acc[e] = w_l * st[e];
     } else {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) o[e] = 0.f;
+      for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
     }
-    if (valid) {
-      for (int s = 0; s < nslots; ++s) {
-        const float ls = slot_lse(s);
-        if (ls == -INFINITY) continue;
-        const float w = fast_exp2(ls - Mz);
-        const float4* src = reinterpret_cast<const float4*>(p.partial + slot_row(s) + c * 32);
+    if (po) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float4 v = src[e];
-          o[4 * e] = fmaf(w, v.x, o[4 * e]);
-          o[4 * e + 1] = fmaf(w, v.y, o[4 * e + 1]);
-          o[4 * e + 2] = fmaf(w, v.z, o[4 * e + 2]);
-          o[4 * e + 3] = fmaf(w, v.w, o[4 * e + 3]);
+      for (int e = 0; e < CPL; ++e) acc[e] = fmaf(w_p, Num<T>::to_f(po[lane * CPL + e]), acc[e]);
+    }
+    float den = w_l + w_p;
+    for (int s0 = 0; s0 < mt.nslots; s0 += 32) {
+      float w = 0.f;
+      if (s0 + lane < mt.nslots) {
+        const float ls = *reinterpret_cast<const float*>(part + (mt.slot + s0 + lane) * sbytes +
+                                                         kTileRows * D * 2 + mt.prow * 4);
+        w = (ls == -INFINITY) ? 0.f : fast_exp2(ls - Mz);
+      }
+      float wsum = w;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+      den += wsum;
+      const int nb = min(32, mt.nslots - s0);
+      for (int j0 = 0; j0 < nb; j0 += 8) {
+        // up to 8 slot rows in flight per lane before any use
+        uint2 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j0 + j < nb) {
+            const uint8_t* src = part + (mt.slot + s0 + j0 + j) * sbytes +
+                                 static_cast<int64_t>(mt.prow) * D * 2 + lane * CPL * 2;
+            if (CPL == 4) {
+              v[j] = *reinterpret_cast<const uint2*>(src);
+            } else {
+              v[j].x = *reinterpret_cast<const uint32_t*>(src);
+              v[j].y = 0u;
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j0 + j < nb) {
+            const float wj = __shfl_sync(0xffffffffu, w, j0 + j);
+            acc[0] = fmaf(wj, __uint_as_float(v[j].x << 16), acc[0]);
+            acc[1 % CPL] = fmaf(wj, __uint_as_float(v[j].x & 0xffff0000u), acc[1 % CPL]);
+            if (CPL == 4) {
+              acc[2 % CPL] = fmaf(wj, __uint_as_float(v[j].y << 16), acc[2 % CPL]);
+              acc[3 % CPL] = fmaf(wj, __uint_as_float(v[j].y & 0xffff0000u), acc[3 % CPL]);
+            }
+          }
         }
       }
-      if (po) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = fmaf(w_p, Num<T>::to_f(po[c * 32 + e]), o[e]);
-      }
-#pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        const uint32_t pr = Fmt<T>::pack(o[e] * factor, o[e + 1] * factor);
-        *reinterpret_cast<uint32_t*>(orow + c * 32 + e) = pr;
-      }
     }
-  }
-  if (valid && p.lse) p.lse[static_cast<int64_t>(tok) * p.l_st + hq] = lse_out;
-
-  if (p.has_local) {
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-      tc_fence_after();
-      tmem_dealloc(tmem, 256);
+    const float lse_out = den > 0.f ? Mz + fast_log2(den) : -INFINITY;
+    float factor = den > 0.f ? 1.f / den : 0.f;
+    if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
+      const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse_out * kLn2 : lse_out) - p.sinks[mt.hq];
+      factor *= 1.f / (1.f + __expf(-x));
     }
-    if (threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
+    T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(mt.tok) * p.o_st +
+              static_cast<int64_t>(mt.hq) * p.o_sh + lane * CPL;
+    if (CPL == 4) {
+      uint2 v;
+      v.x = Fmt<T>::pack(acc[0] * factor, acc[1 % CPL] * factor);
+      v.y = Fmt<T>::pack(acc[2 % CPL] * factor, acc[3 % CPL] * factor);
+      *reinterpret_cast<uint2*>(orow) = v;
+    } else {
+      *reinterpret_cast<uint32_t*>(orow) = Fmt<T>::pack(acc[0] * factor, acc[1 % CPL] * factor);
+    }
+    if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
   }
 }
 
@@ -332,7 +407,7 @@ int launch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMa
       return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured = dev;
   }
-  const int smem = prm.has_local ? C::kSmemBytes : 0;
+  const int smem = C::kSmemBytes;
   suffix_attention_kernel<T, D, NK><<<grid, kThreads, smem, stream>>>(tq, tk, tv, prm);
   return check_launch("suffix_attention_kernel");
 }
@@ -424,15 +499,15 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: head_dim must be 64 or 128");
   if (dtype != D2SD_DTYPE_BF16 && dtype != D2SD_DTYPE_F16)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: dtype must be bf16 or f16");
-  if ((out_stride_head % 2) || (out_stride_token % 2) ||
-      (reinterpret_cast<uintptr_t>(out) & 3u))
-    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: out rows must be 4-byte aligned");
+  if ((out_stride_head % 4) || (out_stride_token % 4) ||
+      (reinterpret_cast<uintptr_t>(out) & 7u))
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: out rows must be 8-byte aligned");
   if (partial && (reinterpret_cast<uintptr_t>(partial) & 15u))
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: partial must be 16-byte aligned");
 
   SuffixParams prm;
   prm.plan = plan;
-  prm.partial = static_cast<const float*>(partial);
+  prm.partial = partial;
   prm.prefix_token = prefix_token;
   prm.prefix_out = partial ? nullptr : prefix_out;
   prm.po_st = prefix_out_stride_token;
@@ -490,12 +565,12 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
       rc = encode_tensor_map(&tv, tdt, v_local, 3, dims, str, box, "v_local");
       if (rc) return rc;
     }
-    grid = dim3(num_blocks, num_kv_heads, (block_len * G + 127) / 128);
+    grid = dim3(num_blocks, num_kv_heads, 2 * ((block_len * G + 127) / 128));
   } else {
     // no level 2: the blocks do not matter, tile all tokens of a head together
     const int64_t ntok = static_cast<int64_t>(num_blocks) * block_len;
     prm.block_len = static_cast<int32_t>(ntok);
-    grid = dim3(1, num_kv_heads, static_cast<unsigned>((ntok * G + 127) / 128));
+    grid = dim3(1, num_kv_heads, static_cast<unsigned>(2 * ((ntok * G + 127) / 128)));
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == D2SD_DTYPE_BF16) return dispatch_suffix<__nv_bfloat16>(tq, tk, tv, prm, head_dim, NK, grid, st);

@@ -92,7 +92,8 @@ int d2sd_prefix_plan(const int32_t* q_tokens, const int32_t* q_token_offset,
                      int32_t num_kv_heads, int32_t num_ctas, int32_t* plan,
                      int64_t capacity, int32_t* num_partial_slots);
 
-/* Bytes of partial state per slot: 128 rows x (head_dim + 1) fp32. */
+/* Bytes of partial state per slot: the normalised O of 128 rows in bf16
+ * ([128][head_dim]) followed by their 128 base-2 LSEs in fp32. */
 int64_t d2sd_partial_slot_bytes(int32_t head_dim);
 
 /* Shared-prefix (level-1) attention on tcgen05/TMEM.

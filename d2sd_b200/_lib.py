@@ -54,6 +54,8 @@ SIGNATURES = {
     "d2sd_verify_accept_workspace_size": (i64, [i32, i32, i64]),
     "d2sd_verify_accept": (i32, [vp, i32, i32, i32, i64, i64, i64, vp, i64, i64, vp, vp, vp, vp,
                                  i64, vp]),
+    "d2sd_verify_accept_noalloc": (i32, [vp, i32, i32, i32, i64, i64, i64, vp, i64, i64, vp,
+                                         vp, vp, vp]),
     "d2sd_commit_kv": (i32, [vp, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64, i64, i32, vp,
                              vp, vp, i64, vp]),
 }

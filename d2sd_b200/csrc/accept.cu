@@ -20,6 +20,9 @@
 // warp that finishes a row's last item (per-row atomic count) reduces the row's
 // partials, and the warp that finishes the last row runs the walk, so no
 // single CTA serialises the reduction.
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 
 namespace d2sd {
@@ -415,4 +418,84 @@ extern "C" int d2sd_verify_accept(const void* logits, int32_t dtype, int32_t num
     default:
       return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: unknown dtype");
   }
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of d2sd_verify_accept.
+//
+// Some callers cannot hand this library a workspace or let it allocate one: a
+// serving runtime whose memory planner owns every device allocation up front
+// (so that peak memory is known and nothing fragments mid-run), or code that
+// runs while a stream is being captured into a CUDA graph, where a cudaMalloc
+// is not allowed. For them the acceptance scratch (the per-CTA argmax records
+// and the completion ticket) lives in the file-scope array below, 256 KiB,
+// which every GPU that loads this library holds until the process exits.
+// Requests whose scratch would not fit are rejected with an error.
+//
+// In host code `g_accept_scratch` is only a host-side stand-in for the device
+// array; its device address is fetched with cudaGetSymbolAddress, once per
+// device, on the first call made with that device current. That first call
+// should therefore happen before any stream capture. All calls share the one
+// array and it keeps the previous call's contents: the ticket is cleared on
+// the caller's stream before every launch, and calls whose kernels overlap on
+// the GPU (e.g. issued on two streams at once) race on the array.
+// ---------------------------------------------------------------------------
+namespace d2sd {
+namespace {
+
+constexpr int64_t kStaticScratchBytes = 256 * 1024;
+static __device__ __align__(256) uint8_t g_accept_scratch[kStaticScratchBytes];
+
+int static_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return fail(D2SD_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept_noalloc: device index above 63");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_accept_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(D2SD_ERR_CUDA, std::string("cudaGetSymbolAddress(g_accept_scratch): ") +
+                                     cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return D2SD_OK;
+}
+
+}  // namespace
+}  // namespace d2sd
+
+extern "C" int d2sd_verify_accept_noalloc(const void* logits, int32_t dtype,
+                                          int32_t num_branches, int32_t block_len, int64_t vocab,
+                                          int64_t stride_branch, int64_t stride_pos,
+                                          const int64_t* block_ids, int64_t ids_stride_branch,
+                                          int64_t ids_stride_pos, int32_t* result,
+                                          int64_t* accepted_ids, int64_t* argmax_out,
+                                          void* stream) {
+  using namespace d2sd;
+  if (num_branches <= 0 || block_len <= 0 || vocab <= 0)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_verify_accept_noalloc: invalid argument");
+  const int64_t need =
+      workspace_bytes(static_cast<int64_t>(num_branches) * block_len, accept_grid());
+  if (need > kStaticScratchBytes)
+    return fail(D2SD_ERR_UNSUPPORTED,
+                "d2sd_verify_accept_noalloc: this shape needs " + std::to_string(need) +
+                    " bytes of scratch; the static scratch array holds " +
+                    std::to_string(kStaticScratchBytes));
+  void* scratch = nullptr;
+  int rc = static_scratch(&scratch);
+  if (rc) return rc;
+  // the completion ticket must start at zero (256 bytes at the array's start)
+  cudaError_t e = cudaMemsetAsync(scratch, 0, 256, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess)
+    return fail(D2SD_ERR_CUDA, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e));
+  return d2sd_verify_accept(logits, dtype, num_branches, block_len, vocab, stride_branch,
+                            stride_pos, block_ids, ids_stride_branch, ids_stride_pos, result,
+                            accepted_ids, argmax_out, scratch, kStaticScratchBytes, stream);
 }

@@ -207,6 +207,23 @@ int d2sd_verify_accept(const void* logits, int32_t dtype,
                        int64_t* accepted_ids, int64_t* argmax_out,
                        void* workspace, int64_t workspace_bytes, void* stream);
 
+/* d2sd_verify_accept without a workspace argument and without allocating.
+ * No counterpart in the reference: it exists for callers that cannot provide
+ * or allocate device memory at call time -- a runtime whose memory planner owns
+ * every allocation, or code running inside a CUDA graph capture. The scratch is
+ * a static 256 KiB device array in the library (held by every GPU that loads
+ * it until exit); shapes needing more are rejected with D2SD_ERR_UNSUPPORTED.
+ * Its device address is looked up on the first call per device, so make that
+ * first call before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race. Other arguments and results as d2sd_verify_accept. */
+int d2sd_verify_accept_noalloc(const void* logits, int32_t dtype,
+                               int32_t num_branches, int32_t block_len,
+                               int64_t vocab, int64_t stride_branch,
+                               int64_t stride_pos, const int64_t* block_ids,
+                               int64_t ids_stride_branch, int64_t ids_stride_pos,
+                               int32_t* result, int64_t* accepted_ids,
+                               int64_t* argmax_out, void* stream);
+
 /* Accepted-branch KV commit for all layers in one launch.
  * layer_ptrs: device array of num_layers*4 pointers
  *   {new_k, new_v, cache_k, cache_v} per layer.

@@ -84,6 +84,34 @@ __device__ __forceinline__ float fast_log2(float x) {
   return y;
 }
 
+// max of three floats in one instruction (PTX max.f32 with three sources).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Packed pairs of fp32 values in one 64-bit register: sm_100 f32x2 arithmetic
+// issues one instruction for two lanes' worth of FMA/ADD.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -137,23 +165,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// try_wait that may suspend the thread for up to hint_ns before returning
-// false; the thread resumes as soon as the phase completes.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity,
-                                                   uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n"
-      "  .reg .pred p;\n"
-      "  mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-      "  selp.u32 %0, 1, 0, p;\n"
-      "}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
 // A wait gives up after this long and raises the CTA's abort flag.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 
@@ -167,7 +178,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 8; ++i) {
-      if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+      if (mbar_try_wait(bar, parity)) return true;
     }
     if (*abort) return false;
     if (global_timer_ns() - t0 > kWaitTimeoutNs) {

@@ -292,24 +292,28 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
       uint32_t s[128];
       tmem_ld128_wait(lane_base + s_col(i), s);
       const int pos0 = t * kTileKeys;
-      if (pos0 < kv_start || pos0 + kTileKeys > kv_end) {  // edge tile: mask invisible keys
+      const bool edge = pos0 < kv_start || pos0 + kTileKeys > kv_end;
+      if (edge) {  // mask invisible keys
 #pragma unroll
         for (int e = 0; e < 128; ++e) {
           const int pos = pos0 + e;
           if (pos < kv_start || pos >= kv_end) s[e] = 0xff800000u;  // -inf
         }
       }
-      // row max with 8 independent accumulators (short dependency chains)
+      // row max: 8 independent accumulators, three-input max
       float mx[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx[e] = __uint_as_float(s[e]);
 #pragma unroll
-      for (int e = 8; e < 128; ++e) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(s[e]));
+      for (int e = 8; e < 128; e += 16) {
 #pragma unroll
-      for (int w = 4; w > 0; w >>= 1) {
-#pragma unroll
-        for (int e = 0; e < w; ++e) mx[e] = fmaxf(mx[e], mx[e + w]);
+        for (int k = 0; k < 8; ++k)
+          mx[k] = fmax3(mx[k], __uint_as_float(s[e + k]), __uint_as_float(s[e + 8 + k]));
       }
+      mx[0] = fmax3(mx[0], mx[1], mx[2]);
+      mx[3] = fmax3(mx[3], mx[4], mx[5]);
+      mx[6] = fmaxf(mx[6], mx[7]);
+      mx[0] = fmax3(mx[0], mx[3], mx[6]);
       const float m_tile = mx[0] * sl2;
       // lazy max: keep m_run unless this tile's max exceeds it by more than 8
       // (p <= 2^8 then); when it does, O and l are rescaled by 2^(m_old - m_new)
@@ -325,18 +329,46 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
       float sm[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) sm[e] = 0.f;
+      if (!edge) {
+        // pairs of columns in f32x2 registers: one FMA / one ADD instruction per pair
+        const uint64_t sc2 = f2_pack(sl2, sl2), nm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, neg_m));
-          const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, neg_m));
-          sm[(2 * e) & 7] += p0;
-          sm[(2 * e + 1) & 7] += p1;
-          pk[e] = pack_bf16x2(p0, p1);
+          for (int e = 0; e < 16; ++e) {
+            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[c * 32 + 2 * e]),
+                                               __uint_as_float(s[c * 32 + 2 * e + 1])), sc2, nm2);
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            const float p0 = fast_exp2(x0);
+            const float p1 = fast_exp2(x1);
+            acc2[e & 3] = f2_add(acc2[e & 3], f2_pack(p0, p1));
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(lane_base + s_col(i) + c * 16, pk);
         }
-        tmem_st16(lane_base + s_col(i) + c * 16, pk);
+        float a0, a1, b0, b1, c0, c1, d0, d1;
+        f2_unpack(acc2[0], a0, a1);
+        f2_unpack(acc2[1], b0, b1);
+        f2_unpack(acc2[2], c0, c1);
+        f2_unpack(acc2[3], d0, d1);
+        sm[0] = a0; sm[1] = a1; sm[2] = b0; sm[3] = b1; sm[4] = c0; sm[5] = c1; sm[6] = d0; sm[7] = d1;
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, neg_m));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, neg_m));
+            sm[(2 * e) & 7] += p0;
+            sm[(2 * e + 1) & 7] += p1;
+            pk[e] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(lane_base + s_col(i) + c * 16, pk);
+        }
       }
       if (f != 1.f) {
         // O holds the sum up to the previous tile: this tile's S commit follows

@@ -190,7 +190,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 
 // ---------------------------------------------------------------------------
 // TMA (tiled tensor copies global -> shared, completion on an mbarrier).
-// Never with a multicast qualifier.
+// Plain (single-CTA destination) copies only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {

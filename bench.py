@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--block", type=int, default=CFG["block"])
     ap.add_argument("--shared", type=int, default=CFG["shared"],
                     help="tokens every branch shares (tree trunk); 0 = independent branches")
+    ap.add_argument("--kv-layout", choices=["umma", "hnd"], default="umma",
+                    help="page format of the target cache (tensor-core order or plain rows)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -69,6 +71,8 @@ def workload_config(a, n):
         "seq_len": a.prefix,
         "parallelism": f"kv-head shard x{n}" if n > 1 else "single GPU",
         "l2": "inputs larger than L2 (paged KV of all layers streamed each step)",
+        "kv_pages": ("16-key pages in tensor-core core-matrix order" if a.kv_layout == "umma"
+                     else "16-key pages of plain rows [page, head, slot, dim]"),
     }
 
 
@@ -262,7 +266,7 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
 
     # --- state resident in HBM -------------------------------------------
-    cache = d.PagedKVCache(L, hk, D, P + T + 16, device=dev,
+    cache = d.PagedKVCache(L, hk, D, P + T + 16, device=dev, layout=a.kv_layout,
                            page_order=torch.randperm(-(-(P + T + 16) // 16),
                                                      generator=torch.Generator().manual_seed(7)))
     cache.k.normal_(generator=g)
@@ -305,7 +309,7 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
         for l in range(L):
             if timing:
                 mark("a0")
-            plan.run_prefix(qs[l], cache.k[l], cache.v[l], "paged_hnd", scale,
+            plan.run_prefix(qs[l], cache.k[l], cache.v[l], cache.kv_layout, scale,
                             page_table=cache.page_table)
             if timing:
                 mark("a1")

@@ -26,6 +26,9 @@ DTYPE_F32 = 0
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
 
+KV_ROWS = 0
+KV_UMMA_PAGES = 1
+
 MASK_NONE = 0
 MASK_CAUSAL = 1
 MASK_CUSTOM = 2
@@ -44,8 +47,8 @@ SIGNATURES = {
     "d2sd_prefix_plan_capacity": (i64, [i32, i32, i32, i32, i64]),
     "d2sd_prefix_plan": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, vp, i64, vp]),
     "d2sd_partial_slot_bytes": (i64, [i32]),
-    "d2sd_prefix_attention": (i32, [vp, i64, i64, i64, vp, vp, i64, i64, i64, i32, i64, vp, vp,
-                                    i32, i32, i32, f32, vp, i32, vp, i64, vp, vp]),
+    "d2sd_prefix_attention": (i32, [vp, i64, i64, i64, vp, vp, i64, i64, i64, i32, i32, i64, vp,
+                                    vp, i32, i32, i32, f32, vp, i32, vp, i64, vp, vp]),
     "d2sd_suffix_merge": (i32, [vp, i64, i64, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp,
                                 vp, i64, i64, vp, i64, vp, i64, i64, vp, i64, vp, i32, i32, i32,
                                 i32, i32, f32, vp, vp]),
@@ -56,8 +59,8 @@ SIGNATURES = {
                                  i64, vp]),
     "d2sd_verify_accept_noalloc": (i32, [vp, i32, i32, i32, i64, i64, i64, vp, i64, i64, vp,
                                          vp, vp, vp]),
-    "d2sd_commit_kv": (i32, [vp, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64, i64, i32, vp,
-                             vp, vp, i64, vp]),
+    "d2sd_commit_kv": (i32, [vp, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64, i64, i32, i32,
+                             vp, vp, vp, i64, vp]),
 }
 
 _lock = threading.Lock()

@@ -9,6 +9,8 @@
 // branch are read on the device from the acceptance kernel's result, so the
 // host never waits between acceptance and commit.
 //
+// Cache formats: D2SD_KV_ROWS (rows contiguous, any page/slot/head strides) and
+// D2SD_KV_UMMA_PAGES (16-key pages in the tensor core's core-matrix order).
 // One 16-byte vector per thread; a row of head_dim elements is handled by
 // head_dim*elem/16 consecutive threads, so each warp moves whole rows with
 // fully coalesced loads and stores.
@@ -22,7 +24,8 @@ constexpr int kThreads = 256;
 __global__ void __launch_bounds__(kThreads)
     commit_kernel(const void* const* __restrict__ layer_ptrs, int L, int Hk, int TB,
                   int vec_per_row, int64_t n_sb, int64_t n_sh, int64_t n_st, int64_t c_sp,
-                  int64_t c_ss, int64_t c_sh, int page_size, const int32_t* __restrict__ page_table,
+                  int64_t c_ss, int64_t c_sh, int page_size, int umma_pages,
+                  const int32_t* __restrict__ page_table,
                   const int32_t* __restrict__ accept_result, const int32_t* __restrict__ len_dev,
                   int64_t len_host, int elem_bytes) {
   const int acc = accept_result[0];
@@ -48,7 +51,12 @@ __global__ void __launch_bounds__(kThreads)
     const int64_t pos = len + t;
     const int64_t pidx = pos / page_size;
     const int64_t page = page_table ? static_cast<int64_t>(page_table[pidx]) : pidx;
-    const int64_t d_off = (page * c_sp + (pos % page_size) * c_ss + h * c_sh) * elem_bytes + vv * 16;
+    const int r = static_cast<int>(pos % page_size);
+    // UMMA pages: 16-byte chunk vv of row r sits in core matrix (r/8, vv), row r%8
+    const int64_t in_page = umma_pages
+                                ? ((static_cast<int64_t>(r / 8) * vec_per_row + vv) * 64 + (r % 8) * 8)
+                                : static_cast<int64_t>(r) * c_ss;
+    const int64_t d_off = (page * c_sp + h * c_sh + in_page) * elem_bytes + (umma_pages ? 0 : vv * 16);
     *reinterpret_cast<uint4*>(dst + d_off) = *reinterpret_cast<const uint4*>(src + s_off);
   }
 }
@@ -61,7 +69,7 @@ extern "C" int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
                               int32_t block_len, int64_t new_stride_branch,
                               int64_t new_stride_head, int64_t new_stride_token,
                               int64_t cache_stride_page, int64_t cache_stride_slot,
-                              int64_t cache_stride_head, int32_t page_size,
+                              int64_t cache_stride_head, int32_t page_size, int32_t cache_format,
                               const int32_t* page_table, const int32_t* accept_result,
                               const int32_t* cache_len_dev, int64_t cache_len_host, void* stream) {
   using namespace d2sd;
@@ -70,6 +78,10 @@ extern "C" int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_commit_kv: invalid argument");
   if (elem_bytes != 2 && elem_bytes != 4)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_commit_kv: elem_bytes must be 2 or 4");
+  if (cache_format != D2SD_KV_ROWS && cache_format != D2SD_KV_UMMA_PAGES)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_commit_kv: unknown cache_format");
+  if (cache_format == D2SD_KV_UMMA_PAGES && (elem_bytes != 2 || page_size != 16))
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_commit_kv: UMMA pages hold 16-bit values, 16 per page");
   if ((static_cast<int64_t>(head_dim) * elem_bytes) % 16 != 0)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_commit_kv: head_dim*elem_bytes must be a multiple of 16");
   const int64_t vec_elems = 16 / elem_bytes;
@@ -85,6 +97,7 @@ extern "C" int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
   commit_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       layer_ptrs, num_layers, num_kv_heads, block_len, vec_per_row, new_stride_branch,
       new_stride_head, new_stride_token, cache_stride_page, cache_stride_slot, cache_stride_head,
-      page_size, page_table, accept_result, cache_len_dev, cache_len_host, elem_bytes);
+      page_size, cache_format == D2SD_KV_UMMA_PAGES ? 1 : 0, page_table, accept_result,
+      cache_len_dev, cache_len_host, elem_bytes);
   return check_launch("commit_kernel");
 }

@@ -285,6 +285,29 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr, uint32_t
   return d;
 }
 
+// Shared-memory matrix descriptor without swizzle (the "interleaved" canonical
+// layout of 8-row x 16-byte core matrices). K-major: lbo = stride between
+// 16-byte K chunks, sbo = stride between 8-row groups. MN-major: sbo = stride
+// between 16-byte MN chunks, lbo = stride between 8-row K groups.
+__device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100); layout 0 = no swizzle
+  return d;
+}
+
+// One-dimensional bulk copy global -> shared (16-byte aligned, size a multiple
+// of 16), completion counted on an mbarrier.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Instruction descriptor of kind::f16 with an f32 accumulator; ab_format 1 =
 // bf16 A and B, 0 = fp16 A and B (A and B always share one type).
 __host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool b_mn_major, uint32_t ab_format) {

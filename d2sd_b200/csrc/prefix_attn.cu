@@ -65,7 +65,14 @@ struct PrefixParams {
   const int32_t* page_table_offset;  // per request
   void* partial;
   int32_t* status;
-  int32_t rows_per_box;  // page_size (paged) or 16 (contiguous)
+  int32_t rows_per_box;  // page_size (paged rows) or 128 (contiguous)
+  // UMMA-native pages: the (page, head) block of 16 keys is stored in the
+  // tensor core's no-swizzle core-matrix order and fetched with one bulk copy
+  const uint8_t* k_pages;
+  const uint8_t* v_pages;
+  int64_t page_stride_bytes;
+  int64_t head_stride_bytes;
+  int num_pages;
   int32_t G;
   float scale_log2;
 };
@@ -87,10 +94,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return ok != 0;
 }
 
-// Producer warp. Lane 0 issues every TMA; the page indices of a KV tile are
-// fetched by the whole warp (lane b reads page b of the tile) one tile ahead
-// of their use, so no TMA waits on a dependent page-table load.
-template <int D>
+// Producer warp. The page indices of a KV tile are fetched by the whole warp
+// (lane b reads page b of the tile) one tile ahead of their use, so no copy
+// waits on a dependent page-table load. Row-layout caches go through TMA tensor
+// boxes issued by lane 0; UMMA-native pages are one bulk copy per page per
+// operand, lane b copying page b.
+template <int D, bool NATIVE>
 __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                          const PrefixParams& p, uint8_t* smem, uint64_t* bars, volatile int* abort,
                          int item_begin, int item_end) {
@@ -145,6 +154,24 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
       if (!alive) break;
       uint8_t* ks = smem + C::kSmemK + s * C::kTileBytes;
       uint8_t* vs = smem + C::kSmemV + s * C::kTileBytes;
+      if (NATIVE) {
+        constexpr uint32_t kPageBlock = 16 * D * 2;  // one page of one head
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&bars[C::B_KFULL + s], C::kTileBytes);
+          mbar_arrive_expect_tx(&bars[C::B_VFULL + s], C::kTileBytes);
+        }
+        __syncwarp();
+        if (lane < boxes) {
+          // a page id outside the pool (a corrupt table) reads page 0 or the last page
+          const int pg = coord < 0 ? 0 : (coord >= p.num_pages ? p.num_pages - 1 : coord);
+          const int64_t off = static_cast<int64_t>(pg) * p.page_stride_bytes +
+                              static_cast<int64_t>(h) * p.head_stride_bytes;
+          bulk_load(ks + lane * kPageBlock, p.k_pages + off, kPageBlock, &bars[C::B_KFULL + s]);
+          bulk_load(vs + lane * kPageBlock, p.v_pages + off, kPageBlock, &bars[C::B_VFULL + s]);
+        }
+        coord = next;
+        continue;
+      }
       if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_KFULL + s], C::kTileBytes);
       for (int b = 0; b < boxes; ++b) {
         const int cb = __shfl_sync(0xffffffffu, coord, b);
@@ -174,35 +201,42 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
   }
 }
 
-template <int D>
+// K in smem: row layout = two 128-byte-swizzled panels of 64 columns; native
+// layout = pages of [2 row groups][D/8 chunks][8 rows][16 B] (no swizzle).
+template <int D, bool NATIVE>
 __device__ __forceinline__ void issue_qk(uint32_t tmem, int i, uint8_t* smem, int stage) {
   using C = Cfg<D>;
   constexpr uint32_t idesc = umma_idesc_bf16(128, 128, false);
+  constexpr uint32_t kGroup = (D / 8) * 128;  // native: bytes per 8-row group
   const uint32_t a0 = smem_u32(smem + C::kSmemQ + i * C::kTileBytes);
   const uint32_t b0 = smem_u32(smem + C::kSmemK + stage * C::kTileBytes);
 #pragma unroll
   for (int ks = 0; ks < D / 16; ++ks) {
     const uint32_t off = (ks / 4) * kPanelBytes + (ks % 4) * 32;
-    umma_ss(tmem + s_col(i), umma_desc_sw128(a0 + off, 16, 1024), umma_desc_sw128(b0 + off, 16, 1024),
-            idesc, ks > 0 ? 1u : 0u);
+    const uint64_t bdesc = NATIVE ? umma_desc_noswz(b0 + ks * 256, 128, kGroup)
+                                  : umma_desc_sw128(b0 + off, 16, 1024);
+    umma_ss(tmem + s_col(i), umma_desc_sw128(a0 + off, 16, 1024), bdesc, idesc, ks > 0 ? 1u : 0u);
   }
 }
 
-template <int D>
+template <int D, bool NATIVE>
 __device__ __forceinline__ void issue_pv(uint32_t tmem, int i, uint8_t* smem, int stage,
                                          bool accumulate) {
   using C = Cfg<D>;
   constexpr uint32_t idesc = umma_idesc_bf16(128, D, true);
+  constexpr uint32_t kGroup = (D / 8) * 128;  // native: bytes per 8-key group
   const uint32_t b0 = smem_u32(smem + C::kSmemV + stage * C::kTileBytes);
 #pragma unroll
   for (int ks = 0; ks < kTileKeys / 16; ++ks) {
-    umma_ts(tmem + o_col(i), tmem + s_col(i) + ks * 8,
-            umma_desc_sw128(b0 + ks * 16 * 128, kPanelBytes, 1024), idesc,
+    // native: one page (16 keys = 2 groups) per K step; MN chunks 16 B apart
+    const uint64_t bdesc = NATIVE ? umma_desc_noswz(b0 + ks * 2 * kGroup, kGroup, 128)
+                                  : umma_desc_sw128(b0 + ks * 16 * 128, kPanelBytes, 1024);
+    umma_ts(tmem + o_col(i), tmem + s_col(i) + ks * 8, bdesc, idesc,
             (accumulate || ks > 0) ? 1u : 0u);
   }
 }
 
-template <int D>
+template <int D, bool NATIVE>
 __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars, uint32_t tmem,
                            volatile int* abort, int item_begin, int item_end) {
   using C = Cfg<D>;
@@ -219,9 +253,9 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
       const int s = static_cast<int>(kt % C::kStages);
       if (!mbar_wait(&bars[C::B_KFULL + s], (kt / C::kStages) & 1, abort)) return;
       tc_fence_after();
-      issue_qk<D>(tmem, 0, smem, s);
+      issue_qk<D, NATIVE>(tmem, 0, smem, s);
       umma_commit(&bars[C::B_SFULL + 0]);
-      issue_qk<D>(tmem, 1, smem, s);
+      issue_qk<D, NATIVE>(tmem, 1, smem, s);
       umma_commit(&bars[C::B_SFULL + 1]);
       if (n == 1) umma_commit(&bars[C::B_QFREE]);
     }
@@ -238,11 +272,11 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
       if (!mbar_wait(&bars[C::B_PFULL + 0], pcount[0] & 1, abort)) return;
       ++pcount[0];
       tc_fence_after();
-      issue_pv<D>(tmem, 0, smem, s, j > 0);
+      issue_pv<D, NATIVE>(tmem, 0, smem, s, j > 0);
       if (has_next) {
         if (!mbar_wait(&bars[C::B_KFULL + sn], ((cur + 1) / C::kStages) & 1, abort)) return;
         tc_fence_after();
-        issue_qk<D>(tmem, 0, smem, sn);
+        issue_qk<D, NATIVE>(tmem, 0, smem, sn);
         umma_commit(&bars[C::B_SFULL + 0]);
       }
       // ---- tile 1 ----
@@ -252,10 +286,10 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
       if (!mbar_wait(&bars[C::B_PFULL + 1], pcount[1] & 1, abort)) return;
       ++pcount[1];
       tc_fence_after();
-      issue_pv<D>(tmem, 1, smem, s, j > 0);
+      issue_pv<D, NATIVE>(tmem, 1, smem, s, j > 0);
       umma_commit(&bars[C::B_KVEMPTY + s]);
       if (has_next) {
-        issue_qk<D>(tmem, 1, smem, sn);
+        issue_qk<D, NATIVE>(tmem, 1, smem, sn);
         umma_commit(&bars[C::B_SFULL + 1]);
         if (j + 2 == n) umma_commit(&bars[C::B_QFREE]);
       }
@@ -422,7 +456,7 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
   }
 }
 
-template <int D>
+template <int D, bool NATIVE>
 __global__ void __launch_bounds__(kNumThreads, 1)
     prefix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
@@ -473,10 +507,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == kTmaWarp) {
-    producer<D>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
+    producer<D, NATIVE>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
     __syncwarp();
   } else if (warp == kMmaWarp) {
-    if (lane == 0) mma_issuer<D>(p, smem, bars, tmem, abort, item_begin, item_end);
+    if (lane == 0) mma_issuer<D, NATIVE>(p, smem, bars, tmem, abort, item_begin, item_end);
     __syncwarp();
   } else {
     softmax_role<D>(p, bars, tmem, abort, item_begin, item_end);
@@ -494,7 +528,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-template <int D>
+template <int D, bool NATIVE>
 int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
            const PrefixParams& prm, int num_ctas, cudaStream_t stream) {
   using C = Cfg<D>;
@@ -502,14 +536,14 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(prefix_attention_kernel<D>,
+    cudaError_t e = cudaFuncSetAttribute(prefix_attention_kernel<D, NATIVE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
     if (e != cudaSuccess)
       return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured_device = dev;
   }
-  prefix_attention_kernel<D><<<num_ctas, kNumThreads, C::kSmemBytes, stream>>>(tq, tk, tv, prm);
+  prefix_attention_kernel<D, NATIVE><<<num_ctas, kNumThreads, C::kSmemBytes, stream>>>(tq, tk, tv, prm);
   return check_launch("prefix_attention_kernel");
 }
 
@@ -523,7 +557,8 @@ extern "C" int64_t d2sd_partial_slot_bytes(int32_t head_dim) {
 extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                                      int64_t num_q_tokens, const void* k, const void* v,
                                      int64_t kv_stride_page, int64_t kv_stride_slot,
-                                     int64_t kv_stride_head, int32_t page_size, int64_t num_pages,
+                                     int64_t kv_stride_head, int32_t page_size, int32_t kv_format,
+                                     int64_t num_pages,
                                      const int32_t* page_table, const int32_t* page_table_offset,
                                      int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
                                      float sm_scale, const int32_t* plan, int32_t num_ctas,
@@ -551,6 +586,12 @@ extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int6
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_prefix_attention: page_table_offset is required");
   if (partial_bytes <= 0)
     return fail(D2SD_ERR_WORKSPACE, "d2sd_prefix_attention: empty partial workspace");
+  const bool native = kv_format == D2SD_KV_UMMA_PAGES;
+  if (kv_format != D2SD_KV_ROWS && !native)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_prefix_attention: unknown kv_format");
+  if (native && (!page_table || page_size != 16))
+    return fail(D2SD_ERR_INVALID_ARGUMENT,
+                "d2sd_prefix_attention: UMMA-native pages need a page table and page_size 16");
 
   CUtensorMap tq, tk, tv;
   {
@@ -562,8 +603,11 @@ extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int6
     int rc = encode_tensor_map(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, q, 3, dims, strides, box, "q");
     if (rc) return rc;
   }
-  int rows_per_box;
-  {
+  int rows_per_box = native ? 16 : 0;
+  if (native) {
+    tk = tq;  // unused by the native-page kernel
+    tv = tq;
+  } else {
     uint64_t dims[4], strides[3];
     uint32_t box[4];
     if (page_table) {
@@ -576,7 +620,7 @@ extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int6
       strides[1] = kv_stride_head * 2;
       strides[2] = kv_stride_page * 2;
     } else {
-      rows_per_box = 16;
+      rows_per_box = 128;
       dims[0] = head_dim;
       dims[1] = num_pages;  // tokens
       dims[2] = num_kv_heads;
@@ -602,9 +646,18 @@ extern "C" int d2sd_prefix_attention(const void* q, int64_t q_stride_token, int6
   prm.partial = partial;
   prm.status = status;
   prm.rows_per_box = rows_per_box;
+  prm.k_pages = static_cast<const uint8_t*>(k);
+  prm.v_pages = static_cast<const uint8_t*>(v);
+  prm.page_stride_bytes = kv_stride_page * 2;
+  prm.head_stride_bytes = kv_stride_head * 2;
+  prm.num_pages = num_pages;
   prm.G = G;
   prm.scale_log2 = sm_scale * kLog2e;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (head_dim == 128) return launch<128>(tq, tk, tv, prm, num_ctas, st);
-  return launch<64>(tq, tk, tv, prm, num_ctas, st);
+  if (native) {
+    return head_dim == 128 ? launch<128, true>(tq, tk, tv, prm, num_ctas, st)
+                           : launch<64, true>(tq, tk, tv, prm, num_ctas, st);
+  }
+  return head_dim == 128 ? launch<128, false>(tq, tk, tv, prm, num_ctas, st)
+                         : launch<64, false>(tq, tk, tv, prm, num_ctas, st);
 }

@@ -8,10 +8,13 @@ holds fixed-capacity page pools instead; ``commit`` moves only the acc accepted
 rows of every layer in one launch, reading acc and the winning branch from the
 acceptance kernel's device result.
 
-Pool layout per layer: [num_pages, Hk, page_size, D] ("HND" pages: one
-contiguous 16 x D block per (page, head), the unit kernel (a) fetches with one
-TMA box). Pools are zero-initialised so every slot past a sequence's length
-holds finite values.
+Pool layout per layer: [num_pages, Hk, 16, D], one contiguous 16 x D block per
+(page, head). With layout="umma" (the default) each block is stored in the
+tensor core's no-swizzle core-matrix order -- [2 groups of 8 rows][D/8 chunks of
+8 elements][8 rows][8 elements] -- so kernel (a) moves a page with one bulk copy
+and feeds it to tcgen05.mma as it lands, whatever the page table's order. With
+layout="hnd" a block holds plain rows (fetched through TMA tensor boxes). Pools
+are zero-initialised so every slot past a sequence's length holds finite values.
 """
 from __future__ import annotations
 
@@ -23,7 +26,12 @@ from . import ops
 class PagedKVCache:
     def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, max_tokens: int,
                  page_size: int = 16, dtype: torch.dtype = torch.bfloat16, device="cuda",
-                 page_order: torch.Tensor | None = None):
+                 page_order: torch.Tensor | None = None, layout: str = "umma"):
+        if layout not in ("umma", "hnd"):
+            raise ValueError("layout must be 'umma' or 'hnd'")
+        if layout == "umma" and (page_size != 16 or head_dim % 8 or dtype.itemsize != 2):
+            raise ValueError("umma pages hold 16 rows of 16-bit values")
+        self.layout = layout
         self.num_layers, self.num_kv_heads, self.head_dim = num_layers, num_kv_heads, head_dim
         self.page_size = page_size
         self.dtype = dtype
@@ -46,7 +54,16 @@ class PagedKVCache:
         """(k_pool, v_pool) of layer l, [num_pages, Hk, page_size, D]."""
         return self.k[l], self.v[l]
 
-    kv_layout = "paged_hnd"
+    @property
+    def kv_layout(self) -> str:
+        return "paged_umma" if self.layout == "umma" else "paged_hnd"
+
+    def _block_view(self, pool: torch.Tensor) -> torch.Tensor:
+        """[L, pages, Hk, 16, D] -> indexable (L, page, head, slot, d) in the
+        core-matrix order: [L, pages, Hk, 2, D/8, 8, 8] permuted to
+        [L, pages, Hk, 2, 8, D/8, 8] = (row group, row, chunk, element)."""
+        L, P, H, S, D = pool.shape
+        return pool.view(L, P, H, 2, D // 8, 8, 8).permute(0, 1, 2, 3, 5, 4, 6)
 
     def positions_to_slots(self, pos: torch.Tensor):
         pt = self.page_table.to(pos.device).long()
@@ -58,15 +75,28 @@ class PagedKVCache:
         n = k.shape[0]
         pos = torch.arange(start, start + n, device=self.device)
         page, slot = self.positions_to_slots(pos)
-        self.k[l, page, :, slot] = k.to(self.dtype)
-        self.v[l, page, :, slot] = v.to(self.dtype)
+        if self.layout == "hnd":
+            self.k[l, page, :, slot] = k.to(self.dtype)
+            self.v[l, page, :, slot] = v.to(self.dtype)
+            return
+        D = self.head_dim
+        for pool, src in ((self.k, k), (self.v, v)):
+            blk = self._block_view(pool)[l]  # [pages, Hk, 2, 8, D/8, 8]
+            blk[page, :, slot // 8, slot % 8] = src.to(self.dtype).view(n, -1, D // 8, 8)
 
     def gather(self, l: int, length: int | None = None):
         """Layer l as contiguous [length, Hk, D] tensors (for checks)."""
         n = self.length if length is None else length
         pos = torch.arange(n, device=self.device)
         page, slot = self.positions_to_slots(pos)
-        return self.k[l, page, :, slot], self.v[l, page, :, slot]
+        if self.layout == "hnd":
+            return self.k[l, page, :, slot], self.v[l, page, :, slot]
+        out = []
+        for pool in (self.k, self.v):
+            blk = self._block_view(pool)[l]
+            out.append(blk[page, :, slot // 8, slot % 8].reshape(n, self.num_kv_heads,
+                                                                   self.head_dim))
+        return out[0], out[1]
 
     # -- kernel (d) ------------------------------------------------------------
     def _layer_ptrs(self, new_k, new_v):
@@ -112,6 +142,7 @@ class PagedKVCache:
                       new_strides=(s[0], s[1], s[2]),
                       cache_strides=(kl.stride(0), kl.stride(2), kl.stride(1)),
                       page_size=self.page_size, page_table=self.page_table,
-                      accept_result=accept_result, cache_len=start)
+                      accept_result=accept_result, cache_len=start,
+                      umma_pages=self.layout == "umma")
         if advance_by is not None:
             self.length = start + int(advance_by)

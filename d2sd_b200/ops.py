@@ -60,7 +60,9 @@ def num_sms(device: torch.device | None = None) -> int:
 class KVView:
     """How kernel (a) addresses a K or V tensor.
 
-    layout "paged_hnd": [pages, Hk, page_size, D]; "paged_nhd": [pages,
+    layout "paged_umma": [pages, Hk, 16, D] holding each (page, head) block in
+    the tensor core's core-matrix order (D2SD_KV_UMMA_PAGES, see
+    kv_cache.PagedKVCache); "paged_hnd": [pages, Hk, page_size, D]; "paged_nhd": [pages,
     page_size, Hk, D]; "nhd": [tokens, Hk, D] (FlashInfer's NHD, the layout of
     generation/verification.py:139-140 after its transpose copy); "hnd":
     [Hk, tokens, D] (a DynamicCache layer [1, Hk, P, D] with the batch index
@@ -74,11 +76,17 @@ class KVView:
     num_kv_heads: int
     head_dim: int
     paged: bool
+    native: bool = False
 
 
 def kv_view(t: torch.Tensor, layout: str) -> KVView:
     if t.stride(-1) != 1:
         raise ValueError("the head dimension of K/V must be contiguous")
+    if layout == "paged_umma":
+        P, H, S, D = t.shape
+        if S != 16 or t.stride(2) != D or t.stride(1) != 16 * D:
+            raise ValueError("paged_umma pools are contiguous [pages, Hk, 16, D] blocks")
+        return KVView(t.stride(0), D, t.stride(1), S, P, H, D, True, True)
     if layout == "paged_hnd":
         P, H, S, D = t.shape
         return KVView(t.stride(0), t.stride(2), t.stride(1), S, P, H, D, True)
@@ -147,7 +155,8 @@ def prefix_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_layou
         raise ValueError("q and k head_dim differ")
     rc = load().d2sd_prefix_attention(
         q.data_ptr(), q.stride(0), q.stride(1), N, k.data_ptr(), v.data_ptr(), kvw.stride_page,
-        kvw.stride_slot, kvw.stride_head, kvw.page_size, kvw.num_pages, _ptr(page_table),
+        kvw.stride_slot, kvw.stride_head, kvw.page_size,
+        _lib.KV_UMMA_PAGES if kvw.native else _lib.KV_ROWS, kvw.num_pages, _ptr(page_table),
         _ptr(page_table_offset), Hq, kvw.num_kv_heads, D, float(sm_scale), plan_dev.data_ptr(),
         int(num_ctas), partial.data_ptr(), partial.numel() * partial.element_size(),
         _ptr(status), _stream(dev))
@@ -251,13 +260,15 @@ def commit_kv(layer_ptrs: torch.Tensor, *, num_layers: int, num_kv_heads: int, h
               elem_bytes: int, block_len: int, new_strides: tuple[int, int, int],
               cache_strides: tuple[int, int, int], page_size: int,
               page_table: torch.Tensor | None, accept_result: torch.Tensor,
-              cache_len_dev: torch.Tensor | None = None, cache_len: int = 0) -> None:
+              cache_len_dev: torch.Tensor | None = None, cache_len: int = 0,
+              umma_pages: bool = False) -> None:
     """Launch kernel (d). layer_ptrs: int64 device tensor [L*4] of
     {new_k, new_v, cache_k, cache_v} pointers; strides in elements:
     new (branch, head, token), cache (page, slot, head)."""
     dev = _require_cuda(layer_ptrs, page_table, accept_result, cache_len_dev)
     rc = load().d2sd_commit_kv(layer_ptrs.data_ptr(), num_layers, num_kv_heads, head_dim,
                                elem_bytes, block_len, *new_strides, *cache_strides, page_size,
+                               _lib.KV_UMMA_PAGES if umma_pages else _lib.KV_ROWS,
                                _ptr(page_table), accept_result.data_ptr(), _ptr(cache_len_dev),
                                int(cache_len), _stream(dev))
     check(rc, "d2sd_commit_kv")

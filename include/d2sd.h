@@ -50,6 +50,18 @@ extern "C" {
 #define D2SD_DTYPE_BF16 1
 #define D2SD_DTYPE_F16 2
 
+/* ---- KV cache formats (d2sd_prefix_attention, d2sd_commit_kv) ---------- */
+/* Rows: a key/value row of head_dim elements is contiguous; pages or tokens,
+ * slots and heads are addressed through the given strides. */
+#define D2SD_KV_ROWS 0
+/* UMMA pages: page_size 16; the 16 x head_dim block of one (page, head) is
+ * stored in the order [2 row groups][head_dim/8 chunks][8 rows][8 elements]
+ * (the tensor core's no-swizzle core-matrix order), so one block is a single
+ * contiguous copy that the tensor core reads in place. Element (page, slot r,
+ * head h, d) sits at page*stride_page + h*stride_head + ((r/8)*(head_dim/8)
+ * + d/8)*64 + (r%8)*8 + d%8. */
+#define D2SD_KV_UMMA_PAGES 1
+
 /* ---- suffix mask modes (d2sd_suffix_merge) ----------------------------- */
 #define D2SD_MASK_NONE 0    /* every block token sees the whole block (DTA) */
 #define D2SD_MASK_CAUSAL 1  /* token t sees tokens 0..t of its block (verify) */
@@ -100,6 +112,8 @@ int64_t d2sd_partial_slot_bytes(int32_t head_dim);
  *
  * q:        bf16 [tokens, num_qo_heads, head_dim], strides in elements
  *           (q_stride_token, q_stride_head), dim stride 1.
+ * kv_format: D2SD_KV_ROWS or D2SD_KV_UMMA_PAGES (then page_table is required,
+ *           page_size is 16 and kv_stride_slot is unused).
  * k, v:     bf16 KV of the prefix. Paged (page_table != NULL): element
  *           (page, slot, head, d) at page*kv_stride_page + slot*kv_stride_slot
  *           + head*kv_stride_head + d, page_size slots per page, num_pages pages;
@@ -123,8 +137,8 @@ int d2sd_prefix_attention(const void* q, int64_t q_stride_token,
                           int64_t q_stride_head, int64_t num_q_tokens,
                           const void* k, const void* v, int64_t kv_stride_page,
                           int64_t kv_stride_slot, int64_t kv_stride_head,
-                          int32_t page_size, int64_t num_pages,
-                          const int32_t* page_table,
+                          int32_t page_size, int32_t kv_format,
+                          int64_t num_pages, const int32_t* page_table,
                           const int32_t* page_table_offset,
                           int32_t num_qo_heads, int32_t num_kv_heads,
                           int32_t head_dim, float sm_scale,
@@ -229,9 +243,11 @@ int d2sd_verify_accept_noalloc(const void* logits, int32_t dtype,
  *   {new_k, new_v, cache_k, cache_v} per layer.
  * new_k/new_v: [num_branches, heads, block_len, head_dim] with element strides
  *   (new_stride_branch, new_stride_head, new_stride_token), dim stride 1.
- * cache: position p of head h at
+ * cache (cache_format D2SD_KV_ROWS): position p of head h at
  *   page_table[p / page_size]*cache_stride_page + (p % page_size)*cache_stride_slot
- *   + h*cache_stride_head (page_table == NULL: page index p / page_size).
+ *   + h*cache_stride_head (page_table == NULL: page index p / page_size);
+ *   (D2SD_KV_UMMA_PAGES): the element order of d2sd_prefix_attention's UMMA
+ *   pages, page_size 16, 16-bit values.
  * accept_result: the device int32[2] {acceptance_length, branch} written by
  *   d2sd_verify_accept; block positions 0..acceptance_length-1 of the winning
  *   branch are written to cache positions cache_len .. cache_len+acc-1, where
@@ -243,7 +259,8 @@ int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
                    int64_t new_stride_head, int64_t new_stride_token,
                    int64_t cache_stride_page, int64_t cache_stride_slot,
                    int64_t cache_stride_head, int32_t page_size,
-                   const int32_t* page_table, const int32_t* accept_result,
+                   int32_t cache_format, const int32_t* page_table,
+                   const int32_t* accept_result,
                    const int32_t* cache_len_dev, int64_t cache_len_host,
                    void* stream);
 

@@ -91,7 +91,7 @@ def test_commit_golden_paged(cuda_device):
         npages = -(-(P + T) // 16) + 2
         g = torch.Generator().manual_seed(i)
         cache = d.PagedKVCache(L, Hk, D, npages * 16, dtype=torch.float32, device=cuda_device,
-                               page_order=torch.randperm(npages, generator=g))
+                               page_order=torch.randperm(npages, generator=g), layout="hnd")
         for l in range(L):
             cache.write(l, torch.from_numpy(cache_k[l, 0]).transpose(0, 1).to(cuda_device),
                         torch.from_numpy(cache_v[l, 0]).transpose(0, 1).to(cuda_device))
@@ -108,13 +108,14 @@ def test_commit_golden_paged(cuda_device):
             np.testing.assert_array_equal(gv.transpose(0, 1).cpu().numpy(), c["out_v"][l, 0])
 
 
-def test_verify_then_commit_device_chain(cuda_device):
+@pytest.mark.parametrize("layout", ["umma", "hnd"])
+def test_verify_then_commit_device_chain(cuda_device, layout):
     """Acceptance result consumed on the device by the commit (no host sync in
     between), all layers in one launch, bf16, strided [B, T, Hk, D] new K/V."""
     import d2sd_b200 as d
     g = torch.Generator().manual_seed(4)
     L, B, T, Hk, D, V, P = 36, 8, 32, 8, 128, 151936, 1000
-    cache = d.PagedKVCache(L, Hk, D, P + T + 16, device=cuda_device,
+    cache = d.PagedKVCache(L, Hk, D, P + T + 16, device=cuda_device, layout=layout,
                            page_order=torch.randperm(-(-(P + T + 16) // 16), generator=g))
     base_k = [torch.randn(P, Hk, D, generator=g).to(torch.bfloat16) for _ in range(L)]
     for l in range(L):

@@ -51,13 +51,15 @@ def test_single_prefill_contiguous(cuda_device, N, P, Hq, Hk, D, layout):
     close(lse, rl, atol=LSE_ATOL)
 
 
+@pytest.mark.parametrize("layout", ["umma", "hnd"])
 @pytest.mark.parametrize("page_order", ["identity", "shuffled"])
 @pytest.mark.parametrize("P,window", [(2048, None), (777, None), (1000, 128), (130, 128)])
-def test_cascade_paged(cuda_device, page_order, P, window):
+@pytest.mark.parametrize("D,Hq", [(128, 32), (64, 64)])
+def test_cascade_paged(cuda_device, layout, page_order, P, window, D, Hq):
     import d2sd_b200 as d
-    B, T, Hq, Hk, D = 4, 16, 32, 8, 128
+    B, T, Hk = 4, 16, 8
     g = torch.Generator().manual_seed(P)
-    cache = d.PagedKVCache(1, Hk, D, max_tokens=P + 64, device=cuda_device,
+    cache = d.PagedKVCache(1, Hk, D, max_tokens=P + 64, device=cuda_device, layout=layout,
                            page_order=(torch.randperm(-(-(P + 64) // 16), generator=g)
                                        if page_order == "shuffled" else None))
     kp = rand((P, Hk, D), g, cuda_device)
@@ -68,8 +70,10 @@ def test_cascade_paged(cuda_device, page_order, P, window):
     kn = rand((B, T, Hk, D), g, cuda_device)
     vn = rand((B, T, Hk, D), g, cuda_device)
     kc, vc = cache.layer(0)
-    out, lse = d.cascade_attention(q, kn, vn, kc, vc, "paged_hnd", P, page_table=cache.page_table,
-                                   sliding_window=window)
+    gk, gv = cache.gather(0, P)
+    assert torch.equal(gk, kp) and torch.equal(gv, vp)
+    out, lse = d.cascade_attention(q, kn, vn, kc, vc, cache.kv_layout, P,
+                                   page_table=cache.page_table, sliding_window=window)
     ro, rl = AT.cascade_attention(f64(q), f64(kn), f64(vn), f64(kp), f64(vp), causal=True,
                                   sliding_window=window)
     close(out, ro)

@@ -40,23 +40,29 @@ template <int D>
 struct Cfg {
   static constexpr int kPanels = D / 64;
   static constexpr int kTileBytes = 128 * D * 2;  // a 128-row Q tile or 128-key K/V tile
-  static constexpr int kStages = (D == 128) ? 2 : 4;
+  // K and V rings are released separately: a K stage as soon as both Q.K^T
+  // products that read it are done, a V stage after both P.V products
+  static constexpr int kKStages = (D == 128) ? 2 : 4;
+  static constexpr int kVStages = (D == 128) ? 2 : 4;
   static constexpr int kSmemQ = 0;
   static constexpr int kSmemK = kSmemQ + 2 * kTileBytes;
-  static constexpr int kSmemV = kSmemK + kStages * kTileBytes;
-  static constexpr int kSmemBar = kSmemV + kStages * kTileBytes;
+  static constexpr int kSmemV = kSmemK + kKStages * kTileBytes;
+  static constexpr int kSmemBar = kSmemV + kVStages * kTileBytes;
   // barrier indices
   static constexpr int B_QFULL = 0;
   static constexpr int B_QFREE = 1;
   static constexpr int B_KFULL = 2;
-  static constexpr int B_VFULL = B_KFULL + kStages;
-  static constexpr int B_KVEMPTY = B_VFULL + kStages;
-  static constexpr int B_SFULL = B_KVEMPTY + kStages;
-  static constexpr int B_PFULL = B_SFULL + 2;
+  static constexpr int B_VFULL = B_KFULL + kKStages;
+  static constexpr int B_KEMPTY = B_VFULL + kVStages;
+  static constexpr int B_VEMPTY = B_KEMPTY + kKStages;
+  static constexpr int B_SFULL = B_VEMPTY + kVStages;
+  static constexpr int B_PHALF = B_SFULL + 2;  // P of keys 0..63 written
+  static constexpr int B_PFULL = B_PHALF + 2;
   static constexpr int B_OFINAL = B_PFULL + 2;
   static constexpr int B_OFREE = B_OFINAL + 2;
   static constexpr int kNumBars = B_OFREE + 2;
   static constexpr int kSmemBytes = kSmemBar + kNumBars * 8 + 16 + 1024;  // + align slack
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
 };
 
 struct PrefixParams {
@@ -146,54 +152,43 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
     alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
     for (int t = t0; t < t1 && alive; ++t, ++kt) {
       const int next = (t + 1 < t1) ? box_coord(t + 1) : 0;  // prefetch the next tile's pages
-      const int s = static_cast<int>(kt % C::kStages);
-      const uint32_t use = kt / C::kStages;
-      if (lane == 0 && use > 0 && !mbar_wait(&bars[C::B_KVEMPTY + s], (use - 1) & 1, abort))
-        alive = false;
-      alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
-      if (!alive) break;
-      uint8_t* ks = smem + C::kSmemK + s * C::kTileBytes;
-      uint8_t* vs = smem + C::kSmemV + s * C::kTileBytes;
-      if (NATIVE) {
-        constexpr uint32_t kPageBlock = 16 * D * 2;  // one page of one head
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&bars[C::B_KFULL + s], C::kTileBytes);
-          mbar_arrive_expect_tx(&bars[C::B_VFULL + s], C::kTileBytes);
-        }
-        __syncwarp();
-        if (lane < boxes) {
-          // a page id outside the pool (a corrupt table) reads page 0 or the last page
-          const int pg = coord < 0 ? 0 : (coord >= p.num_pages ? p.num_pages - 1 : coord);
-          const int64_t off = static_cast<int64_t>(pg) * p.page_stride_bytes +
-                              static_cast<int64_t>(h) * p.head_stride_bytes;
-          bulk_load(ks + lane * kPageBlock, p.k_pages + off, kPageBlock, &bars[C::B_KFULL + s]);
-          bulk_load(vs + lane * kPageBlock, p.v_pages + off, kPageBlock, &bars[C::B_VFULL + s]);
-        }
-        coord = next;
-        continue;
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_KFULL + s], C::kTileBytes);
-      for (int b = 0; b < boxes; ++b) {
-        const int cb = __shfl_sync(0xffffffffu, coord, b);
-        const int c1 = p.page_table ? 0 : cb;
-        const int c3 = p.page_table ? cb : 0;
-        if (lane == 0) {
+      const int sk = static_cast<int>(kt % C::kKStages);
+      const uint32_t uk = kt / C::kKStages;
+      const int sv = static_cast<int>(kt % C::kVStages);
+      const uint32_t uv = kt / C::kVStages;
+      uint8_t* ks = smem + C::kSmemK + sk * C::kTileBytes;
+      uint8_t* vs = smem + C::kSmemV + sv * C::kTileBytes;
+      for (int kv = 0; kv < 2; ++kv) {
+        const int bar_empty = kv ? C::B_VEMPTY + sv : C::B_KEMPTY + sk;
+        const uint32_t use = kv ? uv : uk;
+        uint64_t* full = &bars[kv ? C::B_VFULL + sv : C::B_KFULL + sk];
+        if (lane == 0 && use > 0 && !mbar_wait(&bars[bar_empty], (use - 1) & 1, abort)) alive = false;
+        alive = __shfl_sync(0xffffffffu, alive ? 1 : 0, 0) != 0;
+        if (!alive) break;
+        uint8_t* dst = kv ? vs : ks;
+        if (lane == 0) mbar_arrive_expect_tx(full, C::kTileBytes);
+        if (NATIVE) {
+          constexpr uint32_t kPageBlock = 16 * D * 2;  // one page of one head
+          __syncwarp();
+          if (lane < boxes) {
+            // a page id outside the pool (a corrupt table) reads page 0 or the last page
+            const int pg = coord < 0 ? 0 : (coord >= p.num_pages ? p.num_pages - 1 : coord);
+            const int64_t off = static_cast<int64_t>(pg) * p.page_stride_bytes +
+                                static_cast<int64_t>(h) * p.head_stride_bytes;
+            bulk_load(dst + lane * kPageBlock, (kv ? p.v_pages : p.k_pages) + off, kPageBlock, full);
+          }
+        } else {
+          const CUtensorMap* tm = kv ? tm_v : tm_k;
+          for (int b = 0; b < boxes; ++b) {
+            const int cb = __shfl_sync(0xffffffffu, coord, b);
+            const int c1 = p.page_table ? 0 : cb;
+            const int c3 = p.page_table ? cb : 0;
+            if (lane == 0) {
 #pragma unroll
-          for (int pn = 0; pn < C::kPanels; ++pn)
-            tma_load_4d(ks + pn * kPanelBytes + b * rpb * 128, tm_k, &bars[C::B_KFULL + s],
-                        pn * 64, c1, h, c3);
-        }
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&bars[C::B_VFULL + s], C::kTileBytes);
-      for (int b = 0; b < boxes; ++b) {
-        const int cb = __shfl_sync(0xffffffffu, coord, b);
-        const int c1 = p.page_table ? 0 : cb;
-        const int c3 = p.page_table ? cb : 0;
-        if (lane == 0) {
-#pragma unroll
-          for (int pn = 0; pn < C::kPanels; ++pn)
-            tma_load_4d(vs + pn * kPanelBytes + b * rpb * 128, tm_v, &bars[C::B_VFULL + s],
-                        pn * 64, c1, h, c3);
+              for (int pn = 0; pn < C::kPanels; ++pn)
+                tma_load_4d(dst + pn * kPanelBytes + b * rpb * 128, tm, full, pn * 64, c1, h, c3);
+            }
+          }
         }
       }
       coord = next;
@@ -219,7 +214,7 @@ __device__ __forceinline__ void issue_qk(uint32_t tmem, int i, uint8_t* smem, in
   }
 }
 
-template <int D, bool NATIVE>
+template <int D, bool NATIVE, int KS0, int KS1>
 __device__ __forceinline__ void issue_pv(uint32_t tmem, int i, uint8_t* smem, int stage,
                                          bool accumulate) {
   using C = Cfg<D>;
@@ -227,7 +222,7 @@ __device__ __forceinline__ void issue_pv(uint32_t tmem, int i, uint8_t* smem, in
   constexpr uint32_t kGroup = (D / 8) * 128;  // native: bytes per 8-key group
   const uint32_t b0 = smem_u32(smem + C::kSmemV + stage * C::kTileBytes);
 #pragma unroll
-  for (int ks = 0; ks < kTileKeys / 16; ++ks) {
+  for (int ks = KS0; ks < KS1; ++ks) {
     // native: one page (16 keys = 2 groups) per K step; MN chunks 16 B apart
     const uint64_t bdesc = NATIVE ? umma_desc_noswz(b0 + ks * 2 * kGroup, kGroup, 128)
                                   : umma_desc_sw128(b0 + ks * 16 * 128, kPanelBytes, 1024);
@@ -250,47 +245,56 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
     if (!mbar_wait(&bars[C::B_QFULL], k & 1, abort)) return;
     tc_fence_after();
     {
-      const int s = static_cast<int>(kt % C::kStages);
-      if (!mbar_wait(&bars[C::B_KFULL + s], (kt / C::kStages) & 1, abort)) return;
+      const int sk = static_cast<int>(kt % C::kKStages);
+      if (!mbar_wait(&bars[C::B_KFULL + sk], (kt / C::kKStages) & 1, abort)) return;
       tc_fence_after();
-      issue_qk<D, NATIVE>(tmem, 0, smem, s);
+      issue_qk<D, NATIVE>(tmem, 0, smem, sk);
       umma_commit(&bars[C::B_SFULL + 0]);
-      issue_qk<D, NATIVE>(tmem, 1, smem, s);
+      issue_qk<D, NATIVE>(tmem, 1, smem, sk);
       umma_commit(&bars[C::B_SFULL + 1]);
+      umma_commit(&bars[C::B_KEMPTY + sk]);
       if (n == 1) umma_commit(&bars[C::B_QFREE]);
     }
     for (int j = 0; j < n; ++j) {
       const uint32_t cur = kt + j;
-      const int s = static_cast<int>(cur % C::kStages);
+      const int sv = static_cast<int>(cur % C::kVStages);
       const bool has_next = j + 1 < n;
-      const int sn = static_cast<int>((cur + 1) % C::kStages);
-      if (!mbar_wait(&bars[C::B_VFULL + s], (cur / C::kStages) & 1, abort)) return;
+      const int skn = static_cast<int>((cur + 1) % C::kKStages);
+      if (!mbar_wait(&bars[C::B_VFULL + sv], (cur / C::kVStages) & 1, abort)) return;
       // ---- tile 0 ----
       if (j == 0 && k > 0) {
         if (!mbar_wait(&bars[C::B_OFREE + 0], (k - 1) & 1, abort)) return;
       }
+      // P.V in two halves: keys 0..63 as soon as their P is in TMEM
+      if (!mbar_wait(&bars[C::B_PHALF + 0], pcount[0] & 1, abort)) return;
+      tc_fence_after();
+      issue_pv<D, NATIVE, 0, 4>(tmem, 0, smem, sv, j > 0);
       if (!mbar_wait(&bars[C::B_PFULL + 0], pcount[0] & 1, abort)) return;
       ++pcount[0];
       tc_fence_after();
-      issue_pv<D, NATIVE>(tmem, 0, smem, s, j > 0);
+      issue_pv<D, NATIVE, 4, 8>(tmem, 0, smem, sv, true);
       if (has_next) {
-        if (!mbar_wait(&bars[C::B_KFULL + sn], ((cur + 1) / C::kStages) & 1, abort)) return;
+        if (!mbar_wait(&bars[C::B_KFULL + skn], ((cur + 1) / C::kKStages) & 1, abort)) return;
         tc_fence_after();
-        issue_qk<D, NATIVE>(tmem, 0, smem, sn);
+        issue_qk<D, NATIVE>(tmem, 0, smem, skn);
         umma_commit(&bars[C::B_SFULL + 0]);
       }
       // ---- tile 1 ----
       if (j == 0 && k > 0) {
         if (!mbar_wait(&bars[C::B_OFREE + 1], (k - 1) & 1, abort)) return;
       }
+      if (!mbar_wait(&bars[C::B_PHALF + 1], pcount[1] & 1, abort)) return;
+      tc_fence_after();
+      issue_pv<D, NATIVE, 0, 4>(tmem, 1, smem, sv, j > 0);
       if (!mbar_wait(&bars[C::B_PFULL + 1], pcount[1] & 1, abort)) return;
       ++pcount[1];
       tc_fence_after();
-      issue_pv<D, NATIVE>(tmem, 1, smem, s, j > 0);
-      umma_commit(&bars[C::B_KVEMPTY + s]);
+      issue_pv<D, NATIVE, 4, 8>(tmem, 1, smem, sv, true);
+      umma_commit(&bars[C::B_VEMPTY + sv]);
       if (has_next) {
-        issue_qk<D, NATIVE>(tmem, 1, smem, sn);
+        issue_qk<D, NATIVE>(tmem, 1, smem, skn);
         umma_commit(&bars[C::B_SFULL + 1]);
+        umma_commit(&bars[C::B_KEMPTY + skn]);
         if (j + 2 == n) umma_commit(&bars[C::B_QFREE]);
       }
     }
@@ -360,6 +364,17 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
         m_run = m_tile;
       }
       const float neg_m = -m_run;
+      // keys 0..63 of P are released to the MMA warp before the rest is computed,
+      // unless a lane of this warp must first rescale O (that happens at the end)
+      const bool early = __all_sync(0xffffffffu, f == 1.f);
+      auto release_half = [&](int c) {
+        if (c == 1 && early) {
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars[C::B_PHALF + i]);
+        }
+      };
       float sm[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) sm[e] = 0.f;
@@ -379,9 +394,10 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
             const float p0 = fast_exp2(x0);
             const float p1 = fast_exp2(x1);
             acc2[e & 3] = f2_add(acc2[e & 3], f2_pack(p0, p1));
-            pk[e] = pack_bf16x2(p0, p1);
+            pk[e] = pack_bf16x2_int(p0, p1);
           }
           tmem_st16(lane_base + s_col(i) + c * 16, pk);
+          release_half(c);
         }
         float a0, a1, b0, b1, c0, c1, d0, d1;
         f2_unpack(acc2[0], a0, a1);
@@ -402,6 +418,7 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
             pk[e] = pack_bf16x2(p0, p1);
           }
           tmem_st16(lane_base + s_col(i) + c * 16, pk);
+          release_half(c);
         }
       }
       if (f != 1.f) {
@@ -422,7 +439,10 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[C::B_PFULL + i]);
+      if (lane == 0) {
+        if (!early) mbar_arrive(&bars[C::B_PHALF + i]);
+        mbar_arrive(&bars[C::B_PFULL + i]);
+      }
     }
     // ---- epilogue: normalised O and base-2 LSE into the partial slot ----
     if (!warp_wait(&bars[C::B_OFINAL + i], k & 1, abort)) return;
@@ -477,13 +497,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(&bars[C::B_QFULL], 1);
     mbar_init(&bars[C::B_QFREE], 1);
-    for (int s = 0; s < C::kStages; ++s) {
+    for (int s = 0; s < C::kKStages; ++s) {
       mbar_init(&bars[C::B_KFULL + s], 1);
+      mbar_init(&bars[C::B_KEMPTY + s], 1);
+    }
+    for (int s = 0; s < C::kVStages; ++s) {
       mbar_init(&bars[C::B_VFULL + s], 1);
-      mbar_init(&bars[C::B_KVEMPTY + s], 1);
+      mbar_init(&bars[C::B_VEMPTY + s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[C::B_SFULL + i], 1);
+      mbar_init(&bars[C::B_PHALF + i], 4);
       mbar_init(&bars[C::B_PFULL + i], 4);
       mbar_init(&bars[C::B_OFINAL + i], 1);
       mbar_init(&bars[C::B_OFREE + i], 4);

@@ -305,8 +305,10 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
             e.record(stream)
             ev[name].append(e)
 
-    def step(qs, kns, vns, lg, bid, timing=False):
+    def step(qs, kns, vns, lg, bid, timing=False, wait_layer=None, wait_logits=None):
         for l in range(L):
+            if wait_layer is not None:
+                wait_layer(l)
             if timing:
                 mark("a0")
             plan.run_prefix(qs[l], cache.k[l], cache.v[l], cache.kv_layout, scale,
@@ -323,6 +325,8 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
                 dist.all_gather_into_tensor(gathered, out)
         if timing:
             mark("c0")
+        if wait_logits is not None:
+            wait_logits()
         ver.launch(lg, bid)
         if timing:
             mark("c1")
@@ -399,22 +403,35 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
             h2d += sum(t.numel() * t.element_size() for t in hq_full)
         d2h = h_res.numel() * 4 + h_acc.numel() * 8
 
+        # host->device copies run on their own stream, layer by layer, and
+        # layer l's attention waits only for layer l's inputs: the copies of
+        # later layers (and of the logits) overlap the attention of earlier ones
+        copy_stream = torch.cuda.Stream(dev)
+        ev_layer = [torch.cuda.Event() for _ in range(L)]
+        ev_logits = torch.cuda.Event()
+
         def e2e_step():
-            for l in range(L):
-                d_qp[l].copy_(hq_pref[l], non_blocking=True)
-                if a.shared:
-                    d_qf[l].copy_(hq_full[l], non_blocking=True)
-                d_kn[l].copy_(hkn[l], non_blocking=True)
-                d_vn[l].copy_(hvn[l], non_blocking=True)
-            d_logits.copy_(h_logits, non_blocking=True)
-            d_ids.copy_(h_ids, non_blocking=True)
+            copy_stream.wait_stream(stream)  # after the timer start and the previous step
+            with torch.cuda.stream(copy_stream):
+                for l in range(L):
+                    d_qp[l].copy_(hq_pref[l], non_blocking=True)
+                    if a.shared:
+                        d_qf[l].copy_(hq_full[l], non_blocking=True)
+                    d_kn[l].copy_(hkn[l], non_blocking=True)
+                    d_vn[l].copy_(hvn[l], non_blocking=True)
+                    ev_layer[l].record(copy_stream)
+                d_logits.copy_(h_logits, non_blocking=True)
+                d_ids.copy_(h_ids, non_blocking=True)
+                ev_logits.record(copy_stream)
             nonlocal qs_full
             saved = qs_full
             if a.shared:
                 qs_full = d_qf
             else:
                 qs_full = [t.view(N, hq, D) for t in d_qp]
-            step(d_qp, d_kn, d_vn, d_logits, d_ids)
+            step(d_qp, d_kn, d_vn, d_logits, d_ids,
+                 wait_layer=lambda l: stream.wait_event(ev_layer[l]),
+                 wait_logits=lambda: stream.wait_event(ev_logits))
             qs_full = saved
             h_res.copy_(ver.result, non_blocking=True)
             h_acc.copy_(ver.accepted, non_blocking=True)

@@ -36,6 +36,28 @@ inline bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// Launch kernel<<<grid, block, smem, stream>>>(args...) with programmatic
+// stream serialisation, so that its prologue overlaps the tail of the previous
+// kernel in the stream (the kernel calls grid_dep_wait() before it reads
+// anything that kernel may write).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return fail(D2SD_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return check_launch(what);
+}
+
 // Number of SMs of the current device (cached per device id).
 int current_sm_count();
 
@@ -296,6 +318,18 @@ __device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t smem_addr, uint32_t
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100); layout 0 = no swizzle
   return d;
+}
+
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialisation may start while the previous kernel of its stream still runs;
+// grid_dep_wait() returns once that kernel has completed and its memory is
+// visible (at once for a normal launch). grid_dep_launch() lets the next
+// kernel of the stream start early; kernels here issue it only after their own
+// grid_dep_wait(), so whatever they hand on is ordered after everything that
+// preceded them.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // One-dimensional bulk copy global -> shared (16-byte aligned, size a multiple

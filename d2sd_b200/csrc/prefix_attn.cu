@@ -529,6 +529,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the set-up above overlaps the previous kernel; its outputs (the partial
+  // slots it may still read, the cache it may have written) are safe from here
+  grid_dep_wait();
+  grid_dep_launch();
 
   if (warp == kTmaWarp) {
     producer<D, NATIVE>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
@@ -567,8 +571,8 @@ int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
       return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured_device = dev;
   }
-  prefix_attention_kernel<D, NATIVE><<<num_ctas, kNumThreads, C::kSmemBytes, stream>>>(tq, tk, tv, prm);
-  return check_launch("prefix_attention_kernel");
+  return launch_pdl(prefix_attention_kernel<D, NATIVE>, dim3(num_ctas), dim3(kNumThreads),
+                    C::kSmemBytes, stream, "prefix_attention_kernel", tq, tk, tv, prm);
 }
 
 }  // namespace

@@ -108,7 +108,7 @@ struct RowMeta {
 };
 
 template <typename T, int D, int NK>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 1)
     suffix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
                             const __grid_constant__ CUtensorMap tm_v, const SuffixParams p) {
@@ -138,6 +138,8 @@ __global__ void __launch_bounds__(kThreads)
   const int t = R / G, g = R - (R / G) * G;
   const bool valid = t < TB;
   const int tok = blk * TB + t;
+  // the next kernel may set itself up now; it waits for this one to complete
+  grid_dep_launch();
   if (p.has_local) {
     if (threadIdx.x == 0) {
       for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
@@ -289,6 +291,9 @@ __global__ void __launch_bounds__(kThreads)
   if (p.has_local && threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
 
   // ---- phase 2: merge rows, one warp per row, lanes across columns ----
+  // the partial slots come from the previous kernel (kernel (a)): wait for it.
+  // Phase 1 reads only q and the block's K/V, which precede kernel (a).
+  grid_dep_wait();
   constexpr int CPL = D / 32;  // columns per lane
   const int64_t sbytes = slot_bytes(D);
   const uint8_t* part = static_cast<const uint8_t*>(p.partial);
@@ -403,13 +408,18 @@ int launch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMa
     cudaError_t e = cudaFuncSetAttribute(suffix_attention_kernel<T, D, NK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          C::kSmemBytes);
+    // the shared-memory carve-out kernel (a) runs with: no reconfiguration of
+    // the SMs between the two kernels
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(suffix_attention_kernel<T, D, NK>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess)
       return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured = dev;
   }
-  const int smem = C::kSmemBytes;
-  suffix_attention_kernel<T, D, NK><<<grid, kThreads, smem, stream>>>(tq, tk, tv, prm);
-  return check_launch("suffix_attention_kernel");
+  return launch_pdl(suffix_attention_kernel<T, D, NK>, grid, dim3(kThreads), C::kSmemBytes, stream,
+                    "suffix_attention_kernel", tq, tk, tv, prm);
 }
 
 template <typename T>

@@ -290,93 +290,121 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (p.has_local && threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
 
-  // ---- phase 2: merge rows, one warp per row, lanes across columns ----
+  // ---- phase 2: merge. A warp merges 4 rows at once, 8 lanes per row and
+  // D/8 columns per lane, so that all loads of its rows (every slot LSE and
+  // slot row) are in flight together: one memory round trip per row group ----
   // the partial slots come from the previous kernel (kernel (a)): wait for it.
   // Phase 1 reads only q and the block's K/V, which precede kernel (a).
   grid_dep_wait();
-  constexpr int CPL = D / 32;  // columns per lane
+  constexpr int CPL = D / 8;          // columns per lane
+  constexpr int VEC = CPL * 2 / 16;   // 16-byte vectors per lane and slot row
+  constexpr int kBatch = 8;           // slot rows in flight per lane
+  static_assert(kThreads / 32 * 4 == 64, "16 warps x 4 rows");
   const int64_t sbytes = slot_bytes(D);
   const uint8_t* part = static_cast<const uint8_t*>(p.partial);
-  for (int lr = warp; lr < 64; lr += kThreads / 32) {
-    const RowMeta mt = meta[lr];
-    if (mt.tok < 0) continue;
-    // the row's states: local, dense prefix, or partial slots
-    float lse_p = -INFINITY;
-    const T* po = nullptr;
-    if (!p.partial && p.prefix_out) {
-      po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(mt.tok) * p.po_st +
-           static_cast<int64_t>(mt.hq) * p.po_sh;
-      lse_p = p.prefix_lse[static_cast<int64_t>(mt.tok) * p.pl_st + mt.hq];
-    }
-    float M = fmaxf(mt.lse_local, lse_p);
-    for (int s0 = 0; s0 < mt.nslots; s0 += 32) {
-      float ls = -INFINITY;
-      if (s0 + lane < mt.nslots)
-        ls = *reinterpret_cast<const float*>(part + (mt.slot + s0 + lane) * sbytes +
-                                             kTileRows * D * 2 + mt.prow * 4);
+  const int sub = lane >> 3, j8 = lane & 7;  // row of the warp, lane within the row
+  const int lr = warp * 4 + sub;
+  const RowMeta mt = meta[lr];
+  const bool live = mt.tok >= 0;
+  const int nslots = live ? mt.nslots : 0;
+  // max over the row's 8 lanes (xor 1, 2, 4 stays inside the group)
+  auto gmax = [](float v) {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ls = fmaxf(ls, __shfl_xor_sync(0xffffffffu, ls, o));
-      M = fmaxf(M, ls);
-    }
-    const float Mz = (M == -INFINITY) ? 0.f : M;
-    const float w_l = (mt.lse_local == -INFINITY) ? 0.f : fast_exp2(mt.lse_local - Mz);
-    const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
-    float acc[CPL];
-    if (p.has_local) {
-      const float* st = stage + lr * SP + lane * CPL;
+    for (int o = 1; o < 8; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+  };
+  auto gsum = [](float v) {
 #pragma unroll
-      for (int e = 0; e < CPL; ++e) acc[e] = w_l * st[e];
-    } else {
+    for (int o = 1; o < 8; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+  };
+  const uint8_t* prow_base = part ? part + static_cast<int64_t>(mt.prow) * D * 2 + j8 * CPL * 2
+                                  : nullptr;
+  auto slot_lse = [&](int j) -> float {
+    return *reinterpret_cast<const float*>(part + (mt.slot + j) * sbytes + kTileRows * D * 2 +
+                                           mt.prow * 4);
+  };
+  // first batch: slot LSEs (lane j8 holds slot j8) and the lane's part of up
+  // to kBatch slot rows, all issued before any use
+  float ls = (j8 < nslots) ? slot_lse(j8) : -INFINITY;
+  uint4 v[kBatch][VEC];
 #pragma unroll
-      for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
-    }
-    if (po) {
+  for (int j = 0; j < kBatch; ++j) {
+    if (j < nslots) {
 #pragma unroll
-      for (int e = 0; e < CPL; ++e) acc[e] = fmaf(w_p, Num<T>::to_f(po[lane * CPL + e]), acc[e]);
+      for (int c = 0; c < VEC; ++c)
+        v[j][c] = reinterpret_cast<const uint4*>(prow_base + (mt.slot + j) * sbytes)[c];
     }
-    float den = w_l + w_p;
-    for (int s0 = 0; s0 < mt.nslots; s0 += 32) {
-      float w = 0.f;
-      if (s0 + lane < mt.nslots) {
-        const float ls = *reinterpret_cast<const float*>(part + (mt.slot + s0 + lane) * sbytes +
-                                                         kTileRows * D * 2 + mt.prow * 4);
-        w = (ls == -INFINITY) ? 0.f : fast_exp2(ls - Mz);
+  }
+  // dense prefix state (no partial slots)
+  float lse_p = -INFINITY;
+  const T* po = nullptr;
+  if (live && !p.partial && p.prefix_out) {
+    po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(mt.tok) * p.po_st +
+         static_cast<int64_t>(mt.hq) * p.po_sh + j8 * CPL;
+    lse_p = p.prefix_lse[static_cast<int64_t>(mt.tok) * p.pl_st + mt.hq];
+  }
+  const float lse_local = live ? mt.lse_local : -INFINITY;
+  float M = fmaxf(lse_local, lse_p);
+  M = fmaxf(M, gmax(ls));
+  for (int s0 = 8; s0 < nslots; s0 += 8)  // more than 8 slots: rare
+    M = fmaxf(M, gmax(s0 + j8 < nslots ? slot_lse(s0 + j8) : -INFINITY));
+  const float Mz = (M == -INFINITY) ? 0.f : M;
+  const float w_l = (lse_local == -INFINITY) ? 0.f : fast_exp2(lse_local - Mz);
+  const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
+  float acc[CPL];
+  if (p.has_local && live) {
+    const float4* st = reinterpret_cast<const float4*>(stage + lr * SP + j8 * CPL);
+#pragma unroll
+    for (int e = 0; e < CPL / 4; ++e) {
+      const float4 x = st[e];
+      acc[4 * e] = w_l * x.x;
+      acc[4 * e + 1] = w_l * x.y;
+      acc[4 * e + 2] = w_l * x.z;
+      acc[4 * e + 3] = w_l * x.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
+  }
+  if (po) {
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) acc[e] = fmaf(w_p, Num<T>::to_f(po[e]), acc[e]);
+  }
+  auto add_row = [&](float wj, const uint4 (&r)[VEC]) {
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) {
+      const uint32_t u[4] = {r[c].x, r[c].y, r[c].z, r[c].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc[c * 8 + 2 * k] = fmaf(wj, __uint_as_float(u[k] << 16), acc[c * 8 + 2 * k]);
+        acc[c * 8 + 2 * k + 1] = fmaf(wj, __uint_as_float(u[k] & 0xffff0000u), acc[c * 8 + 2 * k + 1]);
       }
-      float wsum = w;
+    }
+  };
+  float w = (ls == -INFINITY) ? 0.f : fast_exp2(ls - Mz);  // weight of slot j8
+  float den = w_l + w_p + gsum(w);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
-      den += wsum;
-      const int nb = min(32, mt.nslots - s0);
-      for (int j0 = 0; j0 < nb; j0 += 8) {
-        // up to 8 slot rows in flight per lane before any use
-        uint2 v[8];
+  for (int j = 0; j < kBatch; ++j) {
+    const float wj = __shfl_sync(0xffffffffu, w, (lane & ~7) + j);
+    if (j < nslots) add_row(wj, v[j]);
+  }
+  for (int s0 = kBatch; s0 < nslots; s0 += 8) {  // more than 8 slots: rare
+    const float l2 = s0 + j8 < nslots ? slot_lse(s0 + j8) : -INFINITY;
+    const float w2 = (l2 == -INFINITY) ? 0.f : fast_exp2(l2 - Mz);
+    den += gsum(w2);
+    for (int j = 0; j < 8; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w2, (lane & ~7) + j);
+      if (s0 + j < nslots) {
+        uint4 r[VEC];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (j0 + j < nb) {
-            const uint8_t* src = part + (mt.slot + s0 + j0 + j) * sbytes +
-                                 static_cast<int64_t>(mt.prow) * D * 2 + lane * CPL * 2;
-            if (CPL == 4) {
-              v[j] = *reinterpret_cast<const uint2*>(src);
-            } else {
-              v[j].x = *reinterpret_cast<const uint32_t*>(src);
-              v[j].y = 0u;
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (j0 + j < nb) {
-            const float wj = __shfl_sync(0xffffffffu, w, j0 + j);
-            acc[0] = fmaf(wj, __uint_as_float(v[j].x << 16), acc[0]);
-            acc[1 % CPL] = fmaf(wj, __uint_as_float(v[j].x & 0xffff0000u), acc[1 % CPL]);
-            if (CPL == 4) {
-              acc[2 % CPL] = fmaf(wj, __uint_as_float(v[j].y << 16), acc[2 % CPL]);
-              acc[3 % CPL] = fmaf(wj, __uint_as_float(v[j].y & 0xffff0000u), acc[3 % CPL]);
-            }
-          }
-        }
+        for (int c = 0; c < VEC; ++c)
+          r[c] = reinterpret_cast<const uint4*>(prow_base + (mt.slot + s0 + j) * sbytes)[c];
+        add_row(wj, r);
       }
     }
+  }
+  if (live) {
     const float lse_out = den > 0.f ? Mz + fast_log2(den) : -INFINITY;
     float factor = den > 0.f ? 1.f / den : 0.f;
     if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
@@ -384,16 +412,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       factor *= 1.f / (1.f + __expf(-x));
     }
     T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(mt.tok) * p.o_st +
-              static_cast<int64_t>(mt.hq) * p.o_sh + lane * CPL;
-    if (CPL == 4) {
-      uint2 v;
-      v.x = Fmt<T>::pack(acc[0] * factor, acc[1 % CPL] * factor);
-      v.y = Fmt<T>::pack(acc[2 % CPL] * factor, acc[3 % CPL] * factor);
-      *reinterpret_cast<uint2*>(orow) = v;
-    } else {
-      *reinterpret_cast<uint32_t*>(orow) = Fmt<T>::pack(acc[0] * factor, acc[1 % CPL] * factor);
+              static_cast<int64_t>(mt.hq) * p.o_sh + j8 * CPL;
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) {
+      uint4 o;
+      o.x = Fmt<T>::pack(acc[c * 8 + 0] * factor, acc[c * 8 + 1] * factor);
+      o.y = Fmt<T>::pack(acc[c * 8 + 2] * factor, acc[c * 8 + 3] * factor);
+      o.z = Fmt<T>::pack(acc[c * 8 + 4] * factor, acc[c * 8 + 5] * factor);
+      o.w = Fmt<T>::pack(acc[c * 8 + 6] * factor, acc[c * 8 + 7] * factor);
+      reinterpret_cast<uint4*>(orow)[c] = o;
     }
-    if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
+    if (j8 == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
   }
 }
 
@@ -509,9 +538,8 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: head_dim must be 64 or 128");
   if (dtype != D2SD_DTYPE_BF16 && dtype != D2SD_DTYPE_F16)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: dtype must be bf16 or f16");
-  if ((out_stride_head % 4) || (out_stride_token % 4) ||
-      (reinterpret_cast<uintptr_t>(out) & 7u))
-    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: out rows must be 8-byte aligned");
+  if ((out_stride_head % 8) || (out_stride_token % 8) || !aligned16(out))
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: out rows must be 16-byte aligned");
   if (partial && (reinterpret_cast<uintptr_t>(partial) & 15u))
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: partial must be 16-byte aligned");
 

@@ -140,6 +140,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tok = blk * TB + t;
   // the next kernel may set itself up now; it waits for this one to complete
   grid_dep_launch();
+  // ---- row metadata of this CTA's merge half, from the (static) plan: warps
+  // 4-5, idle during the level-2 attention, so the lookups overlap it ----
+  if (warp == 4 || warp == 5) {
+    const int lr = threadIdx.x - 128;
+    const int Rm = rt * 128 + 64 * half + lr;
+    const int tm = Rm / G, gm = Rm - (Rm / G) * G;
+    const bool vm = tm < TB;
+    const int tokm = blk * TB + tm;
+    int slot = 0, nslots = 0, prow = 0;
+    if (vm && p.partial) {
+      const int32_t* pl = p.plan;
+      const int ptok = p.prefix_token ? p.prefix_token[tokm] : tokm;
+      const int req = (ptok >= 0 && ptok < pl[H_NUM_TOKENS]) ? pl[pl[H_OFF_TOKENS] + ptok] : -1;
+      if (req >= 0) {
+        const int32_t* rq = pl + pl[H_OFF_REQUESTS] + req * kReqInts;
+        const int qrow = (ptok - rq[2]) * G + gm;
+        const int32_t* un =
+            pl + pl[H_OFF_UNITS] + (rq[0] + h * rq[1] + qrow / kTileRows) * kUnitInts;
+        slot = un[0];
+        nslots = un[1];
+        prow = qrow % kTileRows;
+      }
+    }
+    // lse_local is written by the warps that own the row's TMEM lane
+    meta[lr].tok = vm ? tokm : -1;
+    meta[lr].hq = h * G + gm;
+    meta[lr].slot = slot;
+    meta[lr].nslots = nslots;
+    meta[lr].prow = prow;
+  }
   if (p.has_local) {
     if (threadIdx.x == 0) {
       for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
@@ -244,28 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- phase 1b: rows of this CTA's merge half: local O -> smem, metadata ----
   if (warp / 2 == half) {  // warps 2*half, 2*half+1 own TMEM lanes [64*half, 64*half+64)
     const int lr = row - 64 * half;
-    RowMeta mt;
-    mt.lse_local = (p.has_local && ok) ? lse_l : -INFINITY;
-    mt.tok = valid ? tok : -1;
-    mt.hq = h * G + g;
-    mt.slot = 0;
-    mt.nslots = 0;
-    mt.prow = 0;
-    if (valid && p.partial) {
-      const int32_t* pl = p.plan;
-      const int ptok = p.prefix_token ? p.prefix_token[tok] : tok;
-      const int req = (ptok >= 0 && ptok < pl[H_NUM_TOKENS]) ? pl[pl[H_OFF_TOKENS] + ptok] : -1;
-      if (req >= 0) {
-        const int32_t* rq = pl + pl[H_OFF_REQUESTS] + req * kReqInts;
-        const int qrow = (ptok - rq[2]) * G + g;
-        const int32_t* un =
-            pl + pl[H_OFF_UNITS] + (rq[0] + h * rq[1] + qrow / kTileRows) * kUnitInts;
-        mt.slot = un[0];
-        mt.nslots = un[1];
-        mt.prow = qrow % kTileRows;
-      }
-    }
-    meta[lr] = mt;
+    meta[lr].lse_local = (p.has_local && ok) ? lse_l : -INFINITY;
     if (p.has_local) {
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
       const float sc = ok ? inv_l : 0.f;

@@ -54,6 +54,8 @@ def parse():
                     help="tokens every branch shares (tree trunk); 0 = independent branches")
     ap.add_argument("--kv-layout", choices=["umma", "hnd"], default="umma",
                     help="page format of the target cache (tensor-core order or plain rows)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="multi-GPU output all-gather: kernel (b)'s own NVLink stores, or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -69,7 +71,9 @@ def workload_config(a, n):
                      f"commit into {a.layers} layers"),
         "global_batch": a.branches * a.block,
         "seq_len": a.prefix,
-        "parallelism": f"kv-head shard x{n}" if n > 1 else "single GPU",
+        "parallelism": (f"kv-head shard x{n}, per-layer output all-gather "
+                        + ("by kernel (b)'s NVLink stores" if a.exchange == "peer" else "by NCCL")
+                        if n > 1 else "single GPU"),
         "l2": "inputs larger than L2 (paged KV of all layers streamed each step)",
         "kv_pages": ("16-key pages in tensor-core core-matrix order" if a.kv_layout == "umma"
                      else "16-key pages of plain rows [page, head, slot, dim]"),
@@ -290,8 +294,10 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
               if a.shared else q[l].reshape(N, hq, D) for l in range(L)]
     out = torch.empty(N, hq, D, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(N, hq, dtype=torch.float32, device=dev)
-    gathered = (torch.empty(world * N, hq, D, dtype=torch.bfloat16, device=dev) if world > 1
-                else None)
+    gathered = (torch.empty(world * N, hq, D, dtype=torch.bfloat16, device=dev)
+                if world > 1 and a.exchange == "nccl" else None)
+    px = (d.PeerExchange(N, Hq, Hk, D, torch.bfloat16, dev)
+          if world > 1 and a.exchange == "peer" else None)
     ver = d.Verifier(B, T, V, dev)
     new_k = kn.transpose(2, 3)  # [L, B, hk, T, D] views of the token-major K/V
     new_v = vn.transpose(2, 3)
@@ -318,10 +324,10 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
             ops.suffix_merge(qs_full[l], kns[l].reshape(N, hk, D), vns[l].reshape(N, hk, D), out,
                              lse, num_blocks=B, block_len=T, num_qo_heads=hq, num_kv_heads=hk,
                              sm_scale=scale, partial=plan.partial, plan_dev=plan.plan,
-                             prefix_token=ptok)
+                             prefix_token=ptok, exchange=px)
             if timing:
                 mark("b1")
-            if world > 1:
+            if gathered is not None:
                 dist.all_gather_into_tensor(gathered, out)
         if timing:
             mark("c0")
@@ -493,6 +499,9 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
         line["cpu_baseline"] = cb
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if px is not None:
+        barrier()  # every rank's kernels are done with the peers' buffers
+        px.close()
 
 
 def main():

@@ -10,6 +10,8 @@ Public surface (mirrors the reference's call surface):
   PagedKVCache                  paged target cache with the accepted-branch commit
   cascade_verify_forward        generation/verification.py:cascade_verify_forward
                                 on these kernels
+  PeerExchange                  KV-head-sharded output all-gather done by kernel (b)'s
+                                own NVLink stores (multi-GPU)
 
 All compute runs in ``libd2sd.so`` (built by ``python -m d2sd_b200.build``);
 importing a kernel entry point without it raises.
@@ -19,11 +21,13 @@ from .cascade import CascadePlan, Request, cascade_attention, shared_trunk_map
 from .flashinfer_compat import merge_state_in_place, single_prefill_with_kv_cache
 from .kv_cache import PagedKVCache
 from .runner import CascadeGraphRunner
+from .sharding import PeerExchange
 
 __all__ = [
     "CascadeGraphRunner",
     "CascadePlan",
     "PagedKVCache",
+    "PeerExchange",
     "Request",
     "Verifier",
     "cascade_attention",

@@ -52,6 +52,13 @@ SIGNATURES = {
     "d2sd_suffix_merge": (i32, [vp, i64, i64, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp,
                                 vp, i64, i64, vp, i64, vp, i64, i64, vp, i64, vp, i32, i32, i32,
                                 i32, i32, f32, vp, vp]),
+    "d2sd_suffix_merge_gather": (i32, [vp, i64, i64, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp,
+                                       vp, vp, i64, i64, vp, i64, vp, i64, i64, vp, i64, vp, i32,
+                                       i32, i32, i32, i32, f32, vp, vp, i32, i32, i32, i64, i64,
+                                       i64, vp, vp]),
+    "d2sd_ipc_handle": (i32, [vp, vp, POINTER(c_int64)]),
+    "d2sd_ipc_open": (i32, [vp, POINTER(c_void_p)]),
+    "d2sd_ipc_close": (i32, [vp]),
     "d2sd_merge_state": (i32, [vp, i64, i64, vp, i64, vp, i64, i64, vp, i64, i64, i32, i32, i32,
                                vp]),
     "d2sd_verify_accept_workspace_size": (i64, [i32, i32, i64]),

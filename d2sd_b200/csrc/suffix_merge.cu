@@ -51,7 +51,19 @@ struct SuffixParams {
   int32_t block_len, mask_mode, sink_mode;
   int32_t Hq, G;
   float scale_log2;
+  // fused output exchange (d2sd_suffix_merge_gather); world == 0: rows go to out
+  void* const* peer_out;
+  unsigned long long* const* peer_ctr;
+  int32_t world, rank, head_offset;
+  int64_t pg_st, pg_sh;
+  int64_t epoch;
 };
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 
 template <int D, int NK>
 struct SCfg {
@@ -420,18 +432,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse_out * kLn2 : lse_out) - p.sinks[mt.hq];
       factor *= 1.f / (1.f + __expf(-x));
     }
-    T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(mt.tok) * p.o_st +
-              static_cast<int64_t>(mt.hq) * p.o_sh + j8 * CPL;
+    uint4 o[VEC];
 #pragma unroll
     for (int c = 0; c < VEC; ++c) {
-      uint4 o;
-      o.x = Fmt<T>::pack(acc[c * 8 + 0] * factor, acc[c * 8 + 1] * factor);
-      o.y = Fmt<T>::pack(acc[c * 8 + 2] * factor, acc[c * 8 + 3] * factor);
-      o.z = Fmt<T>::pack(acc[c * 8 + 4] * factor, acc[c * 8 + 5] * factor);
-      o.w = Fmt<T>::pack(acc[c * 8 + 6] * factor, acc[c * 8 + 7] * factor);
-      reinterpret_cast<uint4*>(orow)[c] = o;
+      o[c].x = Fmt<T>::pack(acc[c * 8 + 0] * factor, acc[c * 8 + 1] * factor);
+      o[c].y = Fmt<T>::pack(acc[c * 8 + 2] * factor, acc[c * 8 + 3] * factor);
+      o[c].z = Fmt<T>::pack(acc[c * 8 + 4] * factor, acc[c * 8 + 5] * factor);
+      o[c].w = Fmt<T>::pack(acc[c * 8 + 6] * factor, acc[c * 8 + 7] * factor);
+    }
+    if (p.world == 0) {
+      T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(mt.tok) * p.o_st +
+                static_cast<int64_t>(mt.hq) * p.o_sh + j8 * CPL;
+#pragma unroll
+      for (int c = 0; c < VEC; ++c) reinterpret_cast<uint4*>(orow)[c] = o[c];
+    } else {
+      // the row into every rank's output, at this rank's head offset (NVLink
+      // stores for the peers)
+      const int64_t off = static_cast<int64_t>(mt.tok) * p.pg_st +
+                          static_cast<int64_t>(p.head_offset + mt.hq) * p.pg_sh + j8 * CPL;
+      for (int d = 0; d < p.world; ++d) {
+        T* orow = static_cast<T*>(p.peer_out[d]) + off;
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) reinterpret_cast<uint4*>(orow)[c] = o[c];
+      }
     }
     if (j8 == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
+  }
+  if (p.world > 0) {
+    // arrival: this CTA's rows are in every rank's buffer. CTA 0 then waits
+    // (bounded) for every CTA of every rank, so that this kernel completes only
+    // when this rank's buffer is whole
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int d = 0; d < p.world; ++d) atomicAdd_system(p.peer_ctr[d], 1ull);
+      if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
+        const unsigned long long expected = static_cast<unsigned long long>(p.epoch) *
+                                            static_cast<unsigned long long>(p.world) * gridDim.x *
+                                            gridDim.y * gridDim.z;
+        const unsigned long long* mine = p.peer_ctr[p.rank];
+        const uint64_t t0 = global_timer_ns();
+        while (ld_acquire_sys(mine) < expected) {
+          if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+            if (p.status) atomicExch(p.status, 3);
+            break;
+          }
+        }
+        __threadfence_system();
+      }
+    }
   }
 }
 
@@ -508,7 +557,15 @@ __global__ void merge_state_kernel(T* v, int64_t v_st, int64_t v_sh, float* s, i
 }  // namespace
 }  // namespace d2sd
 
-extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+namespace d2sd {
+namespace {
+struct PeerArgs {
+  void* const* out_ptrs = nullptr;
+  unsigned long long* const* counters = nullptr;
+  int32_t world = 0, rank = 0, head_offset = 0;
+  int64_t st = 0, sh = 0, epoch = 0;
+};
+int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head,
                                  const void* k_local, const void* v_local, int64_t kv_stride_token,
                                  int64_t kv_stride_head, int32_t num_blocks, int32_t block_len,
                                  int32_t mask_mode, const uint64_t* custom_mask,
@@ -520,8 +577,7 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
                                  float* lse, int64_t lse_stride_token, const float* sinks,
                                  int32_t sink_mode, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim, int32_t dtype, float sm_scale,
-                                 int32_t* status, void* stream) {
-  using namespace d2sd;
+                                 int32_t* status, void* stream, const PeerArgs& pa) {
   if (!out || num_blocks < 0 || block_len <= 0 || num_qo_heads <= 0 || num_kv_heads <= 0 ||
       num_qo_heads % num_kv_heads != 0)
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: invalid argument");
@@ -575,6 +631,14 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
   prm.Hq = num_qo_heads;
   prm.G = G;
   prm.scale_log2 = sm_scale * kLog2e;
+  prm.peer_out = pa.out_ptrs;
+  prm.peer_ctr = pa.counters;
+  prm.world = pa.world;
+  prm.rank = pa.rank;
+  prm.head_offset = pa.head_offset;
+  prm.pg_st = pa.st;
+  prm.pg_sh = pa.sh;
+  prm.epoch = pa.epoch;
 
   CUtensorMap tq, tk, tv;
   std::memset(&tq, 0, sizeof(tq));
@@ -622,6 +686,68 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == D2SD_DTYPE_BF16) return dispatch_suffix<__nv_bfloat16>(tq, tk, tv, prm, head_dim, NK, grid, st);
   return dispatch_suffix<__half>(tq, tk, tv, prm, head_dim, NK, grid, st);
+}
+}  // namespace
+}  // namespace d2sd
+
+extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t q_stride_head,
+                                 const void* k_local, const void* v_local, int64_t kv_stride_token,
+                                 int64_t kv_stride_head, int32_t num_blocks, int32_t block_len,
+                                 int32_t mask_mode, const uint64_t* custom_mask,
+                                 const void* partial, const int32_t* plan,
+                                 const int32_t* prefix_token, const void* prefix_out,
+                                 int64_t prefix_out_stride_token, int64_t prefix_out_stride_head,
+                                 const float* prefix_lse, int64_t prefix_lse_stride_token,
+                                 void* out, int64_t out_stride_token, int64_t out_stride_head,
+                                 float* lse, int64_t lse_stride_token, const float* sinks,
+                                 int32_t sink_mode, int32_t num_qo_heads, int32_t num_kv_heads,
+                                 int32_t head_dim, int32_t dtype, float sm_scale,
+                                 int32_t* status, void* stream) {
+  return d2sd::suffix_merge_impl(q, q_stride_token, q_stride_head, k_local, v_local,
+                                 kv_stride_token, kv_stride_head, num_blocks, block_len, mask_mode,
+                                 custom_mask, partial, plan, prefix_token, prefix_out,
+                                 prefix_out_stride_token, prefix_out_stride_head, prefix_lse,
+                                 prefix_lse_stride_token, out, out_stride_token, out_stride_head,
+                                 lse, lse_stride_token, sinks, sink_mode, num_qo_heads,
+                                 num_kv_heads, head_dim, dtype, sm_scale, status, stream,
+                                 d2sd::PeerArgs{});
+}
+
+extern "C" int d2sd_suffix_merge_gather(
+    const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_local,
+    const void* v_local, int64_t kv_stride_token, int64_t kv_stride_head, int32_t num_blocks,
+    int32_t block_len, int32_t mask_mode, const uint64_t* custom_mask, const void* partial,
+    const int32_t* plan, const int32_t* prefix_token, const void* prefix_out,
+    int64_t prefix_out_stride_token, int64_t prefix_out_stride_head, const float* prefix_lse,
+    int64_t prefix_lse_stride_token, void* out, int64_t out_stride_token, int64_t out_stride_head,
+    float* lse, int64_t lse_stride_token, const float* sinks, int32_t sink_mode,
+    int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim, int32_t dtype, float sm_scale,
+    void* const* out_ptrs, uint64_t* const* counters, int32_t world, int32_t rank,
+    int32_t head_offset, int64_t peer_stride_token, int64_t peer_stride_head, int64_t epoch,
+    int32_t* status, void* stream) {
+  using namespace d2sd;
+  if (!out_ptrs || !counters || world <= 0 || rank < 0 || rank >= world || head_offset < 0 ||
+      epoch <= 0)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge_gather: invalid exchange argument");
+  if (peer_stride_token % 8 || peer_stride_head % 8)
+    return fail(D2SD_ERR_INVALID_ARGUMENT,
+                "d2sd_suffix_merge_gather: output strides must be multiples of 8 elements");
+  PeerArgs pa;
+  pa.out_ptrs = out_ptrs;
+  pa.counters = reinterpret_cast<unsigned long long* const*>(counters);
+  pa.world = world;
+  pa.rank = rank;
+  pa.head_offset = head_offset;
+  pa.st = peer_stride_token;
+  pa.sh = peer_stride_head;
+  pa.epoch = epoch;
+  return suffix_merge_impl(q, q_stride_token, q_stride_head, k_local, v_local, kv_stride_token,
+                           kv_stride_head, num_blocks, block_len, mask_mode, custom_mask, partial,
+                           plan, prefix_token, prefix_out, prefix_out_stride_token,
+                           prefix_out_stride_head, prefix_lse, prefix_lse_stride_token, out,
+                           out_stride_token, out_stride_head, lse, lse_stride_token, sinks,
+                           sink_mode, num_qo_heads, num_kv_heads, head_dim, dtype, sm_scale,
+                           status, stream, pa);
 }
 
 extern "C" int d2sd_merge_state(void* v, int64_t v_stride_token, int64_t v_stride_head, float* s,

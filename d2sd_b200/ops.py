@@ -174,9 +174,13 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
                  plan_dev: torch.Tensor | None = None, prefix_token: torch.Tensor | None = None,
                  prefix_out: torch.Tensor | None = None, prefix_lse: torch.Tensor | None = None,
                  sinks: torch.Tensor | None = None, sink_mode: int = _lib.SINK_NONE,
-                 status: torch.Tensor | None = None) -> None:
+                 status: torch.Tensor | None = None, exchange=None) -> None:
     """Launch kernel (b). Token-major 3-D views: q/out [tokens, Hq, D],
-    k/v_local [tokens, Hk, D], lse/prefix_lse [tokens, Hq]."""
+    k/v_local [tokens, Hk, D], lse/prefix_lse [tokens, Hq].
+
+    exchange: a ``sharding.PeerExchange``; the merged rows then go into every
+    rank's exchange buffer at this rank's head offset (``out`` is not written)
+    and the launch completes once all ranks' rows are in this rank's buffer."""
     dev = _require_cuda(q, k_local, v_local, out, lse, custom_mask, partial, plan_dev,
                         prefix_token, prefix_out, prefix_lse, sinks, status)
     for t in (q, k_local, v_local, out, prefix_out):
@@ -192,7 +196,7 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
     D = out.shape[-1]
     kst = k_local.stride(0) if k_local is not None else 0
     ksh = k_local.stride(1) if k_local is not None else 0
-    rc = load().d2sd_suffix_merge(
+    args = (
         _ptr(q), q.stride(0) if q is not None else 0, q.stride(1) if q is not None else 0,
         _ptr(k_local), _ptr(v_local), kst, ksh, int(num_blocks), int(block_len), int(mask_mode),
         _ptr(custom_mask), _ptr(partial), _ptr(plan_dev), _ptr(prefix_token), _ptr(prefix_out),
@@ -201,8 +205,18 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
         prefix_lse.stride(0) if prefix_lse is not None else 0, out.data_ptr(), out.stride(0),
         out.stride(1), _ptr(lse), lse.stride(0) if lse is not None else 0, _ptr(sinks),
         int(sink_mode), int(num_qo_heads), int(num_kv_heads), int(D), dtype_code(out),
-        float(sm_scale), _ptr(status), _stream(dev))
-    check(rc, "d2sd_suffix_merge")
+        float(sm_scale))
+    if exchange is None:
+        check(load().d2sd_suffix_merge(*args, _ptr(status), _stream(dev)), "d2sd_suffix_merge")
+        return
+    if exchange.buffer.dtype != out.dtype or exchange.buffer.shape[-1] != D:
+        raise ValueError("exchange buffer must match the output dtype and head_dim")
+    epoch = exchange.next_epoch()
+    st = exchange.buffer.stride()
+    check(load().d2sd_suffix_merge_gather(
+        *args, exchange.out_ptrs.data_ptr(), exchange.counter_ptrs.data_ptr(), exchange.world,
+        exchange.rank, int(exchange.head_offset), st[0], st[1], epoch, _ptr(status), _stream(dev)),
+        "d2sd_suffix_merge_gather")
 
 
 def merge_state(v: torch.Tensor, s: torch.Tensor, v_other: torch.Tensor,

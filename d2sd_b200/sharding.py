@@ -100,3 +100,71 @@ class KVHeadShardedAttention:
         out = self.compute(q_local, k_local, v_local, layer)
         dist.all_gather_into_tensor(self.gathered, out.contiguous(), group=self.group)
         return assemble_heads(self.gathered.view(self.world, self.tokens, *self.gathered.shape[1:]))
+
+
+class PeerExchange:
+    """The all-gather of head-sharded attention outputs done by kernel (b)'s own
+    stores over NVLink (``ops.suffix_merge(..., exchange=...)``), in place of
+    ``all_gather_into_tensor`` after it.
+
+    ``buffer`` [tokens, num_qo_heads, head_dim] is this rank's full-width
+    output: rank r's heads land at [r*hq, (r+1)*hq). Each rank exports the
+    buffer and a uint64 arrival counter with CUDA IPC (no multicast objects),
+    opens its peers' and keeps device arrays of the world's pointers. Every
+    rank must call ``suffix_merge`` with the same shapes in the same order, so
+    that the epochs (calls) agree. ``close()`` unmaps the peers' buffers; call
+    it before the process group is destroyed.
+    """
+
+    def __init__(self, tokens: int, num_qo_heads: int, num_kv_heads: int, head_dim: int, dtype,
+                 device, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+        lib = _lib.load()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        hq = qo_head_range(num_qo_heads, num_kv_heads, self.world, self.rank)
+        self.head_offset = hq[0]
+        self.buffer = torch.zeros(tokens, num_qo_heads, head_dim, dtype=dtype, device=device)
+        self.counter = torch.zeros(1, dtype=torch.int64, device=device)
+        mine = []
+        for t in (self.buffer, self.counter):
+            h = ctypes.create_string_buffer(64)
+            off = ctypes.c_int64(0)
+            _lib.check(lib.d2sd_ipc_handle(t.data_ptr(), h, ctypes.byref(off)), "d2sd_ipc_handle")
+            mine.append((h.raw, off.value))
+        allh: list = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        self._opened = []
+        outs, ctrs = [], []
+        for r, handles in enumerate(allh):
+            if r == self.rank:
+                outs.append(self.buffer.data_ptr())
+                ctrs.append(self.counter.data_ptr())
+                continue
+            ptrs = []
+            for raw, off in handles:
+                base = ctypes.c_void_p()
+                _lib.check(lib.d2sd_ipc_open(raw, ctypes.byref(base)), "d2sd_ipc_open")
+                self._opened.append(base.value)
+                ptrs.append(base.value + off)
+            outs.append(ptrs[0])
+            ctrs.append(ptrs[1])
+        self.out_ptrs = torch.tensor(outs, dtype=torch.int64, device=device)
+        self.counter_ptrs = torch.tensor(ctrs, dtype=torch.int64, device=device)
+        self.epoch = 0
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def close(self) -> None:
+        from . import _lib
+        lib = _lib.load()
+        for base in self._opened:
+            _lib.check(lib.d2sd_ipc_close(base), "d2sd_ipc_close")
+        self._opened = []
+

@@ -186,6 +186,52 @@ int d2sd_suffix_merge(const void* q, int64_t q_stride_token,
                       int32_t head_dim, int32_t dtype, float sm_scale,
                       int32_t* status, void* stream);
 
+/* d2sd_suffix_merge with the head-sharded output exchange fused into its
+ * epilogue (KV-head sharding, one process per GPU). It replaces
+ * torch.distributed.all_gather_into_tensor of each rank's attention output
+ * (the one collective of the KV-head-sharded verify step); the reference runs
+ * on one GPU and has no counterpart. Every merged row is stored into the head
+ * slice [head_offset, head_offset + num_qo_heads) of each of the `world` output
+ * buffers out_ptrs[0..world) (this rank's and its peers', peer ones mapped with
+ * d2sd_ipc_open), all with element strides (peer_stride_token,
+ * peer_stride_head); `out` is not written. Each CTA then adds 1 to every
+ * rank's arrival counter counters[r] (uint64, zero before the first call), and
+ * one CTA waits until this rank's counter reaches epoch * world * (number of
+ * CTAs), so the kernel completes only once every rank's rows have landed in
+ * this rank's buffer. epoch counts the calls on these counters (1, 2, ...),
+ * identical on every rank, and every rank must launch the same shapes. The
+ * wait is bounded (2 s); on time-out status receives 3. out_ptrs and counters
+ * are device arrays of device pointers. Rows are stored with 16-byte vectors:
+ * the output bases must be 16-byte aligned and the strides multiples of 8. */
+int d2sd_suffix_merge_gather(const void* q, int64_t q_stride_token,
+                             int64_t q_stride_head, const void* k_local,
+                             const void* v_local, int64_t kv_stride_token,
+                             int64_t kv_stride_head, int32_t num_blocks,
+                             int32_t block_len, int32_t mask_mode,
+                             const uint64_t* custom_mask, const void* partial,
+                             const int32_t* plan, const int32_t* prefix_token,
+                             const void* prefix_out, int64_t prefix_out_stride_token,
+                             int64_t prefix_out_stride_head, const float* prefix_lse,
+                             int64_t prefix_lse_stride_token, void* out,
+                             int64_t out_stride_token, int64_t out_stride_head,
+                             float* lse, int64_t lse_stride_token,
+                             const float* sinks, int32_t sink_mode,
+                             int32_t num_qo_heads, int32_t num_kv_heads,
+                             int32_t head_dim, int32_t dtype, float sm_scale,
+                             void* const* out_ptrs, uint64_t* const* counters,
+                             int32_t world, int32_t rank, int32_t head_offset,
+                             int64_t peer_stride_token, int64_t peer_stride_head,
+                             int64_t epoch, int32_t* status, void* stream);
+
+/* CUDA IPC of a device buffer for the peer exchange: the 64-byte handle of the
+ * allocation holding ptr and ptr's byte offset inside it. */
+int d2sd_ipc_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+/* Maps a peer's handle into this process (peer access enabled on demand);
+ * *base_out receives the allocation's base address here. */
+int d2sd_ipc_open(const void* handle, void** base_out);
+/* Unmaps a base address returned by d2sd_ipc_open. */
+int d2sd_ipc_close(void* base);
+
 /* In-place merge of two attention states (v,s) <- merge((v,s),(v_other,s_other))
  * with base-2 LSEs: v [n, heads, head_dim] (dtype), s [n, heads] fp32. */
 int d2sd_merge_state(void* v, int64_t v_stride_token, int64_t v_stride_head,

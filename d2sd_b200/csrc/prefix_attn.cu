@@ -30,9 +30,19 @@ namespace {
 
 using namespace plan;
 
-constexpr int kNumThreads = 320;
+// 12 warps: two softmax warpgroups (0-7) and a third (8-11) holding the TMA
+// producer (8) and the MMA issuer (9); warps 10-11 only complete that
+// warpgroup. The launch gives every thread kLaunchRegs registers; the third
+// warpgroup then gives most of its share to the softmax warpgroups:
+// 256 x kSoftmaxRegs + 128 x kSideRegs <= 384 x kLaunchRegs.
+constexpr int kNumThreads = 384;
 constexpr int kTmaWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 192;
+constexpr int kSideRegs = 112;
+static_assert(256 * kSoftmaxRegs + 128 * kSideRegs <= kNumThreads * kLaunchRegs,
+              "register split above the launch's registers");
 constexpr int kPanelBytes = 128 * 128;  // 128 rows x 128 bytes (64 bf16)
 constexpr uint32_t kTmemCols = 512;
 
@@ -534,13 +544,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   grid_dep_wait();
   grid_dep_launch();
 
-  if (warp == kTmaWarp) {
-    producer<D, NATIVE>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
-    __syncwarp();
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) mma_issuer<D, NATIVE>(p, smem, bars, tmem, abort, item_begin, item_end);
-    __syncwarp();
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kSideRegs));
+    if (warp == kTmaWarp) {
+      producer<D, NATIVE>(&tm_q, &tm_k, &tm_v, p, smem, bars, abort, item_begin, item_end);
+      __syncwarp();
+    } else if (warp == kMmaWarp) {
+      if (lane == 0) mma_issuer<D, NATIVE>(p, smem, bars, tmem, abort, item_begin, item_end);
+      __syncwarp();
+    }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     softmax_role<D>(p, bars, tmem, abort, item_begin, item_end);
   }
 

@@ -8,9 +8,11 @@
 // normalised O plus the base-2 log-sum-exp lse = m + log2(sum 2^(s*scale*log2e - m)).
 //
 // Design (one persistent CTA per SM, plan_layout.h for the work partition):
-//   warp 8      TMA producer: Q tile pair once per item; per 128-key tile one
-//               2 KB box per page per 64-column panel for K and for V, straight
-//               from the paged cache (no transpose copy), 128-byte swizzle.
+//   warp 8      producer: Q tile pair once per item (TMA); per 128-key tile,
+//               for pages in the tensor core's core-matrix order one bulk copy
+//               per page (lanes 0-7) for K and for V, else TMA boxes straight
+//               from the paged or contiguous cache (128-byte swizzle). K and V
+//               have separate rings and release barriers.
 //   warp 9      MMA issuer (one thread): S_i = Q_i K^T (tcgen05.mma, smem x smem
 //               -> TMEM, M=128 N=128 K=16 steps) and O_i += P_i V (A operand =
 //               P_i in TMEM, B = V in smem, MN-major).
@@ -18,6 +20,9 @@
 //               row = TMEM lane. Online softmax in the log2 domain with a lazy
 //               max (O is rescaled in TMEM only when the running max grows by
 //               more than 8, i.e. a factor 256, which keeps p <= 256 in bf16).
+//               The first 64 keys of P are released to the MMA warp early.
+//   warps 10-11 idle; they complete the third warpgroup, whose registers go
+//               to the softmax warpgroups (setmaxnreg).
 // TMEM: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D); P_i is written
 // as packed bf16 over the first 64 columns of S_i.
 // The two tiles ping-pong: while warpgroup 0 turns S0 into P0 the tensor core

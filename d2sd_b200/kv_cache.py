@@ -114,7 +114,7 @@ class PagedKVCache:
         return ptrs
 
     def commit(self, new_k, new_v, accept_result: torch.Tensor, advance_by: int | None = None,
-               cache_len: int | None = None) -> None:
+               cache_len: int | None = None, target_hidden=None) -> None:
         """Append block positions 0..acc-1 of the winning branch to every layer.
 
         new_k/new_v: per-layer [B, Hk, T, D] tensors (a list, or a stacked
@@ -122,6 +122,13 @@ class PagedKVCache:
         device int32 {acc, branch} of kernel (c). The rows land at positions
         cache_len (default: self.length) onward. ``advance_by`` (the host copy
         of acc, when the caller has read it) moves self.length forward.
+
+        target_hidden: optional (hidden, out). hidden is the list of the draft's
+        selected target layers' hidden states, each [B, T, H] with identical
+        strides (generation/d3_generator.py:239 takes hidden_states[id + 1] for
+        every id of draft.target_layer_ids); out is [T, len(hidden) * H]. The
+        same launch writes out[t] = cat_j(hidden[j][branch, t]) for t < acc,
+        the reference's extract_context_feature(...)[branch, :acc].
         """
         if isinstance(new_k, torch.Tensor):
             new_k = [new_k[l] for l in range(new_k.shape[0])]
@@ -137,12 +144,31 @@ class PagedKVCache:
         if start + T > self.num_pages * self.page_size:
             raise ValueError("cache capacity exceeded")
         kl = self.k[0]
+        hkw = {}
+        if target_hidden is not None:
+            hidden, out = target_hidden
+            hs = hidden[0].stride()
+            for h in hidden:
+                if (h.dim() != 3 or h.shape[:2] != (B, T) or h.stride() != hs or h.stride(-1) != 1
+                        or h.dtype != out.dtype):
+                    raise ValueError("hidden states must be [B, T, H] with identical strides and "
+                                     "the output's dtype")
+            H = hidden[0].shape[-1]
+            if out.shape[0] < T or out.shape[1] != len(hidden) * H:
+                raise ValueError("target_hidden output must be [T, len(hidden) * H]")
+            key = tuple(h.data_ptr() for h in hidden)
+            ptrs = self._ptr_cache.get(("hidden", key))
+            if ptrs is None:
+                ptrs = torch.tensor(list(key), dtype=torch.int64).to(self.device)
+                self._ptr_cache[("hidden", key)] = ptrs
+            hkw = dict(hidden_src_ptrs=ptrs, hidden_size=H, hidden_elem_bytes=out.element_size(),
+                       hidden_strides=(hs[0], hs[1]), hidden_dst=out)
         ops.commit_kv(self._layer_ptrs(new_k, new_v), num_layers=self.num_layers,
                       num_kv_heads=Hk, head_dim=D, elem_bytes=self.k.element_size(), block_len=T,
                       new_strides=(s[0], s[1], s[2]),
                       cache_strides=(kl.stride(0), kl.stride(2), kl.stride(1)),
                       page_size=self.page_size, page_table=self.page_table,
                       accept_result=accept_result, cache_len=start,
-                      umma_pages=self.layout == "umma")
+                      umma_pages=self.layout == "umma", **hkw)
         if advance_by is not None:
             self.length = start + int(advance_by)

@@ -275,14 +275,31 @@ def commit_kv(layer_ptrs: torch.Tensor, *, num_layers: int, num_kv_heads: int, h
               cache_strides: tuple[int, int, int], page_size: int,
               page_table: torch.Tensor | None, accept_result: torch.Tensor,
               cache_len_dev: torch.Tensor | None = None, cache_len: int = 0,
-              umma_pages: bool = False) -> None:
+              umma_pages: bool = False, hidden_src_ptrs: torch.Tensor | None = None,
+              hidden_size: int = 0, hidden_elem_bytes: int = 2,
+              hidden_strides: tuple[int, int] = (0, 0),
+              hidden_dst: torch.Tensor | None = None) -> None:
     """Launch kernel (d). layer_ptrs: int64 device tensor [L*4] of
     {new_k, new_v, cache_k, cache_v} pointers; strides in elements:
-    new (branch, head, token), cache (page, slot, head)."""
-    dev = _require_cuda(layer_ptrs, page_table, accept_result, cache_len_dev)
-    rc = load().d2sd_commit_kv(layer_ptrs.data_ptr(), num_layers, num_kv_heads, head_dim,
-                               elem_bytes, block_len, *new_strides, *cache_strides, page_size,
-                               _lib.KV_UMMA_PAGES if umma_pages else _lib.KV_ROWS,
-                               _ptr(page_table), accept_result.data_ptr(), _ptr(cache_len_dev),
-                               int(cache_len), _stream(dev))
-    check(rc, "d2sd_commit_kv")
+    new (branch, head, token), cache (page, slot, head).
+
+    With hidden_src_ptrs (int64 device tensor of the selected layers' hidden
+    state pointers, each [branches, block, hidden_size] with element strides
+    hidden_strides = (branch, token)), the same launch also writes
+    hidden_dst[t] = cat_j(hidden_j[branch, t]) for t < acc (the draft's
+    context feature)."""
+    dev = _require_cuda(layer_ptrs, page_table, accept_result, cache_len_dev, hidden_src_ptrs,
+                        hidden_dst)
+    args = (layer_ptrs.data_ptr(), num_layers, num_kv_heads, head_dim, elem_bytes, block_len,
+            *new_strides, *cache_strides, page_size,
+            _lib.KV_UMMA_PAGES if umma_pages else _lib.KV_ROWS, _ptr(page_table),
+            accept_result.data_ptr(), _ptr(cache_len_dev), int(cache_len))
+    if hidden_src_ptrs is None:
+        check(load().d2sd_commit_kv(*args, _stream(dev)), "d2sd_commit_kv")
+        return
+    if hidden_dst is None or hidden_dst.dim() != 2 or hidden_dst.stride(1) != 1:
+        raise ValueError("hidden_dst must be [block, num_hidden * hidden_size], rows contiguous")
+    check(load().d2sd_commit_kv_hidden(
+        *args, hidden_src_ptrs.data_ptr(), int(hidden_src_ptrs.numel()), int(hidden_size),
+        int(hidden_elem_bytes), int(hidden_strides[0]), int(hidden_strides[1]),
+        hidden_dst.data_ptr(), hidden_dst.stride(0), _stream(dev)), "d2sd_commit_kv_hidden")

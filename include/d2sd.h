@@ -26,6 +26,10 @@
  *       form generation/dflash_generator.py:110-125.
  *   d2sd_commit_kv
  *       the accepted-branch KV append generation/d3_generator.py:227-232.
+ *   d2sd_commit_kv_hidden
+ *       the same, fused with the draft's context-feature gather
+ *       generation/d3_generator.py:239 (model/utils.py:17-26,
+ *       extract_context_feature, indexed [valid_block, :acceptance_length]).
  */
 #ifndef D2SD_H_
 #define D2SD_H_
@@ -309,6 +313,34 @@ int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
                    const int32_t* accept_result,
                    const int32_t* cache_len_dev, int64_t cache_len_host,
                    void* stream);
+
+/* d2sd_commit_kv fused with the gather of the draft model's context feature
+ * for the same (branch, positions 0..acc-1) index set, in the same launch:
+ *   hidden_dst[t, j*hidden_size + c] = hidden_src[j][branch, t, c]
+ * for t < acceptance_length, j < num_hidden, c < hidden_size, i.e. the
+ * reference's torch.cat of the selected layers' hidden states along the last
+ * axis, row-sliced by the winning branch and the accepted length. Rows
+ * t >= acceptance_length of hidden_dst are not written.
+ * hidden_src: device array of num_hidden pointers, each [num_branches,
+ *   block_len, hidden_size] with element strides (hidden_stride_branch,
+ *   hidden_stride_token), last axis contiguous; hidden_dst: [block_len,
+ *   num_hidden*hidden_size] with row stride hidden_dst_stride_token.
+ * hidden_elem_bytes is 2 or 4; hidden_size*hidden_elem_bytes and every stride
+ * in bytes must be multiples of 16, the pointers 16-byte aligned. */
+int d2sd_commit_kv_hidden(const void* const* layer_ptrs, int32_t num_layers,
+                          int32_t num_kv_heads, int32_t head_dim,
+                          int32_t elem_bytes, int32_t block_len,
+                          int64_t new_stride_branch, int64_t new_stride_head,
+                          int64_t new_stride_token, int64_t cache_stride_page,
+                          int64_t cache_stride_slot, int64_t cache_stride_head,
+                          int32_t page_size, int32_t cache_format,
+                          const int32_t* page_table, const int32_t* accept_result,
+                          const int32_t* cache_len_dev, int64_t cache_len_host,
+                          const void* const* hidden_src, int32_t num_hidden,
+                          int32_t hidden_size, int32_t hidden_elem_bytes,
+                          int64_t hidden_stride_branch,
+                          int64_t hidden_stride_token, void* hidden_dst,
+                          int64_t hidden_dst_stride_token, void* stream);
 
 #ifdef __cplusplus
 }

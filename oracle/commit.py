@@ -40,3 +40,15 @@ def commit_paged(pool_k, pool_v, page_table, cache_len: int, new_k, new_v, branc
             pool_k[page, slot] = new_k[branch, :, t]
             pool_v[page, slot] = new_v[branch, :, t]
     return pool_k, pool_v
+
+
+def context_feature(hidden_states, layer_ids, branch: int, acc: int):
+    """generation/d3_generator.py:239 with model/utils.py:17-26.
+
+    extract_context_feature concatenates hidden_states[id + 1] (the +1 skips
+    the embedding output) of every selected layer id along the last axis; the
+    generator keeps the winning branch's first acc rows:
+    [acc, len(layer_ids) * H] (the reference adds a leading unit axis).
+    """
+    sel = [hidden_states[i + 1] for i in layer_ids]
+    return np.concatenate(sel, axis=-1)[branch, :acc]

@@ -10,13 +10,18 @@ What is executed from the reference (catnanami/D2-SD), unmodified:
     reference's model/utils.py:sample;
   * single-branch acceptance: generation/dflash_generator.py:110-120;
   * KV commit: generation/d3_generator.py:227-232 on a transformers DynamicCache;
+  * draft context feature: the assignment at generation/d3_generator.py:239
+    (state.target_hidden = extract_context_feature(...)[valid_block,
+    :acceptance_length, :].unsqueeze(0)) with the reference's
+    model/utils.py:extract_context_feature (written to hidden_cases.npz;
+    `--only hidden` regenerates that file alone);
   * attention: generation/verification.py:cascade_verify_forward on tiny random
     Qwen3 and GPT-OSS models, with flashinfer's two kernels (which need a GPU)
     replaced by the float64 oracle, and the Qwen3 logits checked against the
     reference's plain_verify_forward (HF sdpa, an independent attention). The
     attention output each layer feeds o_proj is recorded as the golden value.
 
-Usage: python tests/golden/make_golden.py
+Usage: python tests/golden/make_golden.py [--only hidden]
 """
 from __future__ import annotations
 
@@ -186,6 +191,28 @@ def gen_commit_cases(rng: np.random.Generator):
     return cases
 
 
+def gen_hidden_cases(rng: np.random.Generator):
+    from model.utils import extract_context_feature
+    line = next(l for l in (REF / "generation/d3_generator.py").read_text().splitlines()
+                if "state.target_hidden = extract_context_feature" in l and "valid_block" in l)
+    block = textwrap.dedent(line)
+    cases = []
+    for (L, B, T, H, ids) in ((6, 3, 8, 32, (1, 3, 4)), (4, 8, 32, 16, (0, 2)),
+                              (3, 1, 16, 16, (1,)), (8, 4, 16, 8, (0, 3, 5, 6))):
+        for acc in sorted({1, T // 2, T}):
+            branch = int(rng.integers(0, B))
+            hs = [rng.standard_normal((B, T, H)).astype(np.float32) for _ in range(L + 2)]
+            ns = dict(extract_context_feature=extract_context_feature,
+                      output=SimpleNamespace(hidden_states=[torch.from_numpy(h) for h in hs]),
+                      draft=SimpleNamespace(target_layer_ids=list(ids)),
+                      valid_block=torch.tensor(branch), acceptance_length=acc,
+                      state=SimpleNamespace())
+            exec(block, ns)
+            cases.append(dict(hidden=np.stack(hs), layer_ids=np.asarray(ids), branch=branch,
+                              acc=acc, out=ns["state"].target_hidden.numpy()))
+    return cases
+
+
 # --------------------------------------------------------------------------
 # attention through the reference's cascade_verify_forward
 # --------------------------------------------------------------------------
@@ -309,6 +336,11 @@ def save_cases(path: Path, cases, keys):
 
 def main():
     ver, sample = import_reference()
+    hd_cases = gen_hidden_cases(np.random.default_rng(20261202))
+    save_cases(HERE / "hidden_cases.npz", hd_cases, ["hidden", "layer_ids", "branch", "acc", "out"])
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "hidden":
+        print(json.dumps({"hidden_cases": len(hd_cases)}))
+        return
     rng = np.random.default_rng(20260101)
     acc_cases = gen_accept_cases(sample, rng)
     save_cases(HERE / "accept_cases.npz", acc_cases,
@@ -319,7 +351,7 @@ def main():
     save_cases(HERE / "commit_cases.npz", cm_cases,
                ["L", "branch", "acc", "cache_k", "cache_v", "new_k", "new_v", "out_k", "out_v"])
     summary = {"accept_cases": len(acc_cases), "dflash_cases": len(df_cases),
-               "commit_cases": len(cm_cases)}
+               "commit_cases": len(cm_cases), "hidden_cases": len(hd_cases)}
     for kind, P, B, T in (("qwen3", 300, 3, 8), ("gptoss", 300, 3, 8)):
         layers, s = gen_attention_case(ver, kind, P, B, T)
         save_cases(HERE / f"attention_{kind}.npz", layers,

@@ -143,3 +143,61 @@ def test_verify_then_commit_device_chain(cuda_device, layout):
                                       branch, acc)
         np.testing.assert_array_equal(gk.float().transpose(0, 1).cpu().numpy(), ok[0][0])
         np.testing.assert_array_equal(gv.float().transpose(0, 1).cpu().numpy(), ov[0][0])
+
+
+def test_commit_with_context_feature_golden(cuda_device):
+    """The context-feature gather fused into the commit launch against the
+    reference's extract_context_feature(...)[valid_block, :acceptance_length]
+    (generation/d3_generator.py:239), fp32 hidden states, bit for bit; the KV
+    commit of the same launch is checked against the oracle."""
+    import d2sd_b200 as d
+    g = torch.Generator().manual_seed(12)
+    for c in load_cases("hidden_cases.npz"):
+        hidden = torch.from_numpy(c["hidden"])  # [L + 2, B, T, H]
+        ids = [int(i) for i in c["layer_ids"]]
+        branch, acc = int(c["branch"]), int(c["acc"])
+        _, B, T, H = hidden.shape
+        Hk, D, P = 2, 16, 40
+        cache = d.PagedKVCache(1, Hk, D, P + T + 16, dtype=torch.float32, device=cuda_device,
+                               layout="hnd")
+        base = torch.randn(P, Hk, D, generator=g)
+        cache.write(0, base.to(cuda_device), base.to(cuda_device))
+        cache.length = P
+        nk = torch.randn(1, B, Hk, T, D, generator=g)
+        src = [hidden[i + 1].to(cuda_device) for i in ids]
+        out = torch.full((T, len(ids) * H), -7.0, device=cuda_device)
+        res = torch.tensor([acc, branch], dtype=torch.int32, device=cuda_device)
+        cache.commit(nk.to(cuda_device), nk.to(cuda_device), res, advance_by=acc,
+                     target_hidden=(src, out))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out[:acc].cpu().numpy(), c["out"][0])
+        assert bool((out[acc:] == -7.0).all())
+        gk, gv = cache.gather(0)
+        ok, _ = OC.commit_contiguous([base.transpose(0, 1)[None].numpy()],
+                                     [base.transpose(0, 1)[None].numpy()],
+                                     [(nk[0].numpy(), nk[0].numpy())], branch, acc)
+        np.testing.assert_array_equal(gk.transpose(0, 1).cpu().numpy(), ok[0][0])
+
+
+def test_verify_commit_context_feature_chain(cuda_device):
+    """bf16 hidden states [B, T, H] at Qwen3-8B width (H 4096) and three draft
+    layers, acc and branch read on the device from kernel (c)."""
+    import d2sd_b200 as d
+    g = torch.Generator().manual_seed(13)
+    L, B, T, Hk, D, V, P, H = 2, 8, 16, 8, 128, 4096, 256, 4096
+    cache = d.PagedKVCache(L, Hk, D, P + T + 16, device=cuda_device)
+    cache.length = P
+    nk = torch.randn(L, B, Hk, T, D, generator=g).to(torch.bfloat16).to(cuda_device)
+    z = torch.randn(B, T, V, generator=g).to(torch.bfloat16)
+    x = torch.randint(0, V, (B, T), generator=g)
+    x[:, 1:] = torch.where(torch.rand(B, T - 1, generator=g) < 0.8, z.float().argmax(-1)[:, :-1],
+                           x[:, 1:])
+    hs = [torch.randn(B, T, H, generator=g).to(torch.bfloat16).to(cuda_device) for _ in range(5)]
+    ids = [0, 2, 3]
+    out = torch.zeros(T, len(ids) * H, dtype=torch.bfloat16, device=cuda_device)
+    ver = d.Verifier(B, T, V, cuda_device)
+    ver.launch(z.to(cuda_device), x.to(cuda_device))
+    cache.commit(nk, nk, ver.result, target_hidden=([hs[i + 1] for i in ids], out))
+    acc, _, branch = ver.read()
+    ref = OC.context_feature([h.float().cpu().numpy() for h in hs], ids, branch, acc)
+    np.testing.assert_array_equal(out[:acc].float().cpu().numpy(), ref)

@@ -140,3 +140,12 @@ def test_torch_masked_sdpa_matches_cascade():
     o2, l2 = AT.cascade_attention(q, kn, vn, kp, vp, causal=True)
     np.testing.assert_allclose(o1.numpy(), o2, atol=1e-5)
     np.testing.assert_allclose(l1.numpy(), l2, atol=1e-5)
+
+
+def test_context_feature_oracle_matches_reference():
+    cases = load_cases("hidden_cases.npz")
+    assert len(cases) >= 10
+    for c in cases:
+        got = OC.context_feature(list(c["hidden"]), [int(i) for i in c["layer_ids"]],
+                                 int(c["branch"]), int(c["acc"]))
+        np.testing.assert_array_equal(got[None], c["out"])

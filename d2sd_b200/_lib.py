@@ -68,6 +68,8 @@ SIGNATURES = {
                                          vp, vp, vp]),
     "d2sd_commit_kv": (i32, [vp, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64, i64, i32, i32,
                              vp, vp, vp, i64, vp]),
+    "d2sd_qk_norm_rope": (i32, [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i64, i64, i32, i32,
+                                i32, i32, i32, vp, vp, f32, vp, vp, i64, i32, vp, vp]),
     "d2sd_commit_kv_hidden": (i32, [vp, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64, i64, i32,
                                     i32, vp, vp, vp, i64, vp, i32, i32, i32, i64, i64, vp, i64,
                                     vp]),

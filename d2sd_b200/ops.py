@@ -303,3 +303,41 @@ def commit_kv(layer_ptrs: torch.Tensor, *, num_layers: int, num_kv_heads: int, h
         *args, hidden_src_ptrs.data_ptr(), int(hidden_src_ptrs.numel()), int(hidden_size),
         int(hidden_elem_bytes), int(hidden_strides[0]), int(hidden_strides[1]),
         hidden_dst.data_ptr(), hidden_dst.stride(0), _stream(dev)), "d2sd_commit_kv_hidden")
+
+
+# ---------------------------------------------------------------------------
+# QK-norm + RoPE of the block's q and k (the step before (a)/(b))
+# ---------------------------------------------------------------------------
+def qk_norm_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *,
+                 q_weight: torch.Tensor | None = None, k_weight: torch.Tensor | None = None,
+                 eps: float = 1e-6, block_len: int | None = None,
+                 positions: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
+                 k_out: torch.Tensor | None = None):
+    """q [tokens, Hq, D], k [tokens, Hk, D] (token-major views, head_dim
+    contiguous); cos/sin [positions, D or D/2] in the data dtype; q_weight /
+    k_weight the per-head RMSNorm weights [D] (Qwen3) or None (GPT-OSS).
+    Tokens are branch-major blocks of block_len tokens (default: all tokens one
+    block); token t uses table row positions[t % block_len] (default t % block_len).
+    Writes q_out/k_out (default: in place) and returns them."""
+    dev = _require_cuda(q, k, cos, sin, q_weight, k_weight, positions, q_out, k_out)
+    q_out = q if q_out is None else q_out
+    k_out = k if k_out is None else k_out
+    for t in (q, k, q_out, k_out):
+        if t.dim() != 3 or t.stride(-1) != 1:
+            raise ValueError("q/k must be [tokens, heads, head_dim] with head_dim contiguous")
+    if q.dtype != k.dtype or cos.dtype != q.dtype or sin.dtype != q.dtype:
+        raise ValueError("q, k, cos and sin must share a dtype")
+    if cos.stride() != sin.stride() or cos.stride(-1) != 1:
+        raise ValueError("cos and sin must share strides, columns contiguous")
+    if positions is not None and positions.dtype != torch.int32:
+        raise ValueError("positions must be int32")
+    n, hq, D = q.shape
+    bl = n if block_len is None else int(block_len)
+    check(load().d2sd_qk_norm_rope(
+        q.data_ptr(), q.stride(0), q.stride(1), q_out.data_ptr(), q_out.stride(0), q_out.stride(1),
+        k.data_ptr(), k.stride(0), k.stride(1), k_out.data_ptr(), k_out.stride(0),
+        k_out.stride(1), n, hq, k.shape[1], D, dtype_code(q), _ptr(q_weight), _ptr(k_weight),
+        float(eps), cos.data_ptr(), sin.data_ptr(), cos.stride(0), bl, _ptr(positions),
+        _stream(dev)), "d2sd_qk_norm_rope")
+    return q_out, k_out
+

@@ -3,8 +3,9 @@
 Same signature and results as generation/verification.py:49-201 of the
 reference: a manual layer-by-layer forward of a HuggingFace Qwen3 or GPT-OSS
 target over B candidate blocks that share one cached prefix. The projections,
-norms, RoPE, MLP and lm_head stay PyTorch (cuBLAS); the attention of every
-layer is one launch of kernel (a) over the cache in place -- the DynamicCache
+MLP and lm_head stay PyTorch (cuBLAS); the QK-norm and RoPE of each layer's
+block q and k are one launch of d2sd_qk_norm_rope (:113-124); the attention of
+every layer is one launch of kernel (a) over the cache in place -- the DynamicCache
 layer [1, Hk, P, D] read as an HND tensor, so the reference's per-layer
 transpose copy of the whole prefix (:139-140) is gone -- and one launch of
 kernel (b) for the per-branch causal attention, the LSE merge and, for GPT-OSS,
@@ -20,29 +21,8 @@ from types import SimpleNamespace
 
 import torch
 
+from . import ops
 from .cascade import CascadePlan, Request, cascade_attention
-
-
-def _rotate_half(x):
-    x1, x2 = x.chunk(2, dim=-1)
-    return torch.cat((-x2, x1), dim=-1)
-
-
-def _rope_qwen3(q, k, cos, sin):
-    """cos/sin [bsz, seq, head_dim] with duplicated halves (verification.py:21-28)."""
-    cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
-    return q * cos + _rotate_half(q) * sin, k * cos + _rotate_half(k) * sin
-
-
-def _rope_gpt_oss(q, k, cos, sin):
-    """cos/sin [bsz, seq, head_dim/2] applied to the two halves (verification.py:31-42)."""
-    cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
-
-    def ap(x):
-        a, b = torch.chunk(x, 2, dim=-1)
-        return torch.cat([a * cos - b * sin, b * cos + a * sin], dim=-1)
-
-    return ap(q), ap(k)
 
 
 def _layer_kv(past_key_values, idx):
@@ -59,10 +39,9 @@ def cascade_verify_forward(target_model, input_ids: torch.Tensor, position_ids: 
     model = target_model.model
     bsz, seq_len = input_ids.shape
     is_gpt_oss = type(model.layers[0].self_attn).__name__ == "GptOssAttention"
-    rope = _rope_gpt_oss if is_gpt_oss else _rope_qwen3
-
     hidden = model.embed_tokens(input_ids)
-    cos, sin = model.rotary_emb(hidden, position_ids)
+    cos, sin = model.rotary_emb(hidden, position_ids)  # [1, block, D] (GPT-OSS: D/2)
+    cos_t, sin_t = cos[0].contiguous(), sin[0].contiguous()
     all_hidden = [hidden] if output_hidden_states else None
     new_kv_list = []
     plans: dict = {}
@@ -77,10 +56,14 @@ def cascade_verify_forward(target_model, input_ids: torch.Tensor, position_ids: 
         q = attn.q_proj(h).view(bsz, seq_len, Hq, D)
         k_new = attn.k_proj(h).view(bsz, seq_len, Hk, D)
         v_new = attn.v_proj(h).view(bsz, seq_len, Hk, D)
-        if not is_gpt_oss:
-            q = attn.q_norm(q)
-            k_new = attn.k_norm(k_new)
-        q, k_new = rope(q.transpose(1, 2), k_new.transpose(1, 2), cos, sin)
+        # QK-norm (Qwen3) and RoPE in place on the token-major [B*T, H, D] views
+        norm = not is_gpt_oss
+        ops.qk_norm_rope(q.view(bsz * seq_len, Hq, D), k_new.view(bsz * seq_len, Hk, D), cos_t,
+                         sin_t, q_weight=attn.q_norm.weight if norm else None,
+                         k_weight=attn.k_norm.weight if norm else None,
+                         eps=attn.q_norm.variance_epsilon if norm else 1e-6, block_len=seq_len)
+        q = q.transpose(1, 2)
+        k_new = k_new.transpose(1, 2)
         v_new = v_new.transpose(1, 2)
         new_kv_list.append((k_new, v_new))
 

@@ -26,6 +26,11 @@
  *       form generation/dflash_generator.py:110-125.
  *   d2sd_commit_kv
  *       the accepted-branch KV append generation/d3_generator.py:227-232.
+ *   d2sd_qk_norm_rope
+ *       the step before the attention, generation/verification.py:113-124:
+ *       attn.q_norm / attn.k_norm (transformers' Qwen3RMSNorm; skipped for
+ *       GPT-OSS) and rope_apply (_apply_rotary_pos_emb_qwen3 :21-28 or
+ *       _apply_rotary_pos_emb_gpt_oss :31-43) on the block's q and k.
  *   d2sd_commit_kv_hidden
  *       the same, fused with the draft's context-feature gather
  *       generation/d3_generator.py:239 (model/utils.py:17-26,
@@ -313,6 +318,31 @@ int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
                    const int32_t* accept_result,
                    const int32_t* cache_len_dev, int64_t cache_len_host,
                    void* stream);
+
+/* Per-head RMSNorm (optional) and rotary embedding of the block's q and k in
+ * one launch, with the 16-bit roundings of the reference's eager expressions:
+ *   y = rnd(w * rnd(x * rsqrt(mean(x^2) + eps)))   (when q_weight/k_weight given)
+ *   out = rnd(rnd(y * cos) + rnd(rotate_half(y) * sin)).
+ * q_in/q_out: [num_tokens, num_qo_heads, head_dim], k_in/k_out: [num_tokens,
+ * num_kv_heads, head_dim], element strides (token, head), head_dim contiguous;
+ * out may alias in. q_weight/k_weight: [head_dim] in the data dtype, both or
+ * neither (GPT-OSS). cos_table/sin_table: [positions, >= head_dim/2] with row
+ * stride table_stride, read through their first head_dim/2 columns (a
+ * full-width Qwen3 table has equal halves; GPT-OSS's is half-width). Token t
+ * takes row positions[t % block_len] (positions == NULL: t % block_len), the
+ * block position shared by every branch. dtype bf16 or f16, head_dim 64 or 128. */
+int d2sd_qk_norm_rope(const void* q_in, int64_t q_in_stride_token,
+                      int64_t q_in_stride_head, void* q_out,
+                      int64_t q_out_stride_token, int64_t q_out_stride_head,
+                      const void* k_in, int64_t k_in_stride_token,
+                      int64_t k_in_stride_head, void* k_out,
+                      int64_t k_out_stride_token, int64_t k_out_stride_head,
+                      int32_t num_tokens, int32_t num_qo_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                      const void* q_weight, const void* k_weight, float eps,
+                      const void* cos_table, const void* sin_table,
+                      int64_t table_stride, int32_t block_len,
+                      const int32_t* positions, void* stream);
 
 /* d2sd_commit_kv fused with the gather of the draft model's context feature
  * for the same (branch, positions 0..acc-1) index set, in the same launch:

@@ -15,13 +15,17 @@ What is executed from the reference (catnanami/D2-SD), unmodified:
     :acceptance_length, :].unsqueeze(0)) with the reference's
     model/utils.py:extract_context_feature (written to hidden_cases.npz;
     `--only hidden` regenerates that file alone);
+  * QK-norm + RoPE: generation/verification.py:113-124 restated with the
+    reference's own _apply_rotary_pos_emb_qwen3 / _apply_rotary_pos_emb_gpt_oss
+    and transformers' Qwen3RMSNorm on bf16 tensors (rope_cases.npz;
+    `--only rope` regenerates that file alone);
   * attention: generation/verification.py:cascade_verify_forward on tiny random
     Qwen3 and GPT-OSS models, with flashinfer's two kernels (which need a GPU)
     replaced by the float64 oracle, and the Qwen3 logits checked against the
     reference's plain_verify_forward (HF sdpa, an independent attention). The
     attention output each layer feeds o_proj is recorded as the golden value.
 
-Usage: python tests/golden/make_golden.py [--only hidden]
+Usage: python tests/golden/make_golden.py [--only hidden|rope]
 """
 from __future__ import annotations
 
@@ -213,6 +217,43 @@ def gen_hidden_cases(rng: np.random.Generator):
     return cases
 
 
+def gen_rope_cases(ver, rng: np.random.Generator):
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+    cases = []
+    for kind, B, T, Hq, Hk, D in (("qwen3", 3, 8, 8, 2, 128), ("qwen3", 2, 16, 4, 4, 64),
+                                  ("gptoss", 3, 8, 8, 2, 64)):
+        bf = lambda *shape: torch.from_numpy(  # noqa: E731
+            rng.standard_normal(shape).astype(np.float32)).to(torch.bfloat16)
+        q, k = bf(B, T, Hq, D) * 3, bf(B, T, Hk, D) * 3
+        pos = np.arange(T) + int(rng.integers(0, 5000))
+        inv = 1.0 / (1e6 ** (np.arange(0, D, 2) / D))
+        ang = pos[:, None] * inv[None, :]
+        half_c = torch.from_numpy(np.cos(ang).astype(np.float32)).to(torch.bfloat16)
+        half_s = torch.from_numpy(np.sin(ang).astype(np.float32)).to(torch.bfloat16)
+        entry = dict(kind=np.asarray(kind), q=q.view(torch.int16).numpy(),
+                     k=k.view(torch.int16).numpy(), cos_half=half_c.view(torch.int16).numpy(),
+                     sin_half=half_s.view(torch.int16).numpy())
+        if kind == "qwen3":
+            qn, kn = Qwen3RMSNorm(D, eps=1e-6), Qwen3RMSNorm(D, eps=1e-6)
+            qn.weight.data = (1 + 0.1 * bf(D).float()).to(torch.bfloat16)
+            kn.weight.data = (1 + 0.1 * bf(D).float()).to(torch.bfloat16)
+            qn, kn = qn.to(torch.bfloat16), kn.to(torch.bfloat16)
+            cos = torch.cat([half_c, half_c], -1)[None]
+            sin = torch.cat([half_s, half_s], -1)[None]
+            with torch.no_grad():
+                qq, kk = ver._apply_rotary_pos_emb_qwen3(qn(q).transpose(1, 2),
+                                                         kn(k).transpose(1, 2), cos, sin)
+            entry.update(q_weight=qn.weight.data.view(torch.int16).numpy(),
+                         k_weight=kn.weight.data.view(torch.int16).numpy())
+        else:
+            qq, kk = ver._apply_rotary_pos_emb_gpt_oss(q.transpose(1, 2), k.transpose(1, 2),
+                                                       half_c[None], half_s[None])
+        entry.update(q_out=qq.transpose(1, 2).contiguous().view(torch.int16).numpy(),
+                     k_out=kk.transpose(1, 2).contiguous().view(torch.int16).numpy())
+        cases.append(entry)
+    return cases
+
+
 # --------------------------------------------------------------------------
 # attention through the reference's cascade_verify_forward
 # --------------------------------------------------------------------------
@@ -340,6 +381,12 @@ def main():
     save_cases(HERE / "hidden_cases.npz", hd_cases, ["hidden", "layer_ids", "branch", "acc", "out"])
     if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "hidden":
         print(json.dumps({"hidden_cases": len(hd_cases)}))
+        return
+    rp_cases = gen_rope_cases(ver, np.random.default_rng(20261203))
+    save_cases(HERE / "rope_cases.npz", rp_cases,
+               ["kind", "q", "k", "cos_half", "sin_half", "q_weight", "k_weight", "q_out", "k_out"])
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "rope":
+        print(json.dumps({"rope_cases": len(rp_cases)}))
         return
     rng = np.random.default_rng(20260101)
     acc_cases = gen_accept_cases(sample, rng)

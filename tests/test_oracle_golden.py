@@ -149,3 +149,21 @@ def test_context_feature_oracle_matches_reference():
         got = OC.context_feature(list(c["hidden"]), [int(i) for i in c["layer_ids"]],
                                  int(c["branch"]), int(c["acc"]))
         np.testing.assert_array_equal(got[None], c["out"])
+
+
+def test_rope_oracle_matches_reference():
+    import torch
+    from oracle import rope as OR
+    cases = load_cases("rope_cases.npz")
+    assert len(cases) >= 3
+    bf = lambda a: torch.from_numpy(a).view(torch.bfloat16)  # noqa: E731
+    for c in cases:
+        gpt = str(c["kind"]) == "gptoss"
+        ch, sh = bf(c["cos_half"]), bf(c["sin_half"])
+        cos = ch[None] if gpt else torch.cat([ch, ch], -1)[None]
+        sin = sh[None] if gpt else torch.cat([sh, sh], -1)[None]
+        qw = None if gpt else bf(c["q_weight"])
+        kw = None if gpt else bf(c["k_weight"])
+        q, k = OR.qk_norm_rope(bf(c["q"]), bf(c["k"]), cos, sin, qw, kw, 1e-6, gpt_oss=gpt)
+        assert torch.equal(q.contiguous().view(torch.int16), torch.from_numpy(c["q_out"]))
+        assert torch.equal(k.contiguous().view(torch.int16), torch.from_numpy(c["k_out"]))

@@ -37,10 +37,9 @@ def tiny(kind, dev):
 def oracle_forward(model, ids, pos, cache, is_gpt_oss):
     """The reference's layer loop (generation/verification.py:96-201) with the
     attention computed by the float64 oracle of the same cascade."""
-    from d2sd_b200.verification import _rope_gpt_oss, _rope_qwen3
+    from oracle import rope as OR
     m = model.model
     B, T = ids.shape
-    rope = _rope_gpt_oss if is_gpt_oss else _rope_qwen3
     h = m.embed_tokens(ids)
     cos, sin = m.rotary_emb(h, pos)
     for li, layer in enumerate(m.layers):
@@ -51,9 +50,11 @@ def oracle_forward(model, ids, pos, cache, is_gpt_oss):
         q = at.q_proj(x).view(B, T, Hq, D)
         k = at.k_proj(x).view(B, T, Hk, D)
         v = at.v_proj(x).view(B, T, Hk, D)
-        if not is_gpt_oss:
-            q, k = at.q_norm(q), at.k_norm(k)
-        q, k = rope(q.transpose(1, 2), k.transpose(1, 2), cos, sin)
+        qw = None if is_gpt_oss else at.q_norm.weight
+        kw = None if is_gpt_oss else at.k_norm.weight
+        q, k = OR.qk_norm_rope(q, k, cos, sin, qw, kw, 1e-6 if is_gpt_oss else at.q_norm.variance_epsilon,
+                               gpt_oss=is_gpt_oss)
+        q, k = q.transpose(1, 2), k.transpose(1, 2)
         v = v.transpose(1, 2)
         kp = cache.layers[li].keys[0].transpose(0, 1)
         vp = cache.layers[li].values[0].transpose(0, 1)

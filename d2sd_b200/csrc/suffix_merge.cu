@@ -50,6 +50,7 @@ struct SuffixParams {
   int32_t has_local;
   int32_t block_len, mask_mode, sink_mode;
   int32_t Hq, G;
+  int32_t rows_per_cta;  // merge rows of a CTA: 64, 32 or 16 (128-row tile / parts)
   float scale_log2;
   // fused output exchange (d2sd_suffix_merge_gather); world == 0: rows go to out
   void* const* peer_out;
@@ -136,7 +137,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* stage = reinterpret_cast<float*>(smem + C::kSmemQ);  // reuses Q after the MMAs
 
   const int blk = blockIdx.x, h = blockIdx.y;
-  const int rt = blockIdx.z >> 1, half = blockIdx.z & 1;  // 128-row tile, 64-row merge half
+  // 128-row tile rt, merge part `part` = rows [part*RP, part*RP + RP) of it
+  const int RP = p.rows_per_cta;
+  const int parts = kTileRows / RP;
+  const int rt = blockIdx.z / parts, part = blockIdx.z - (blockIdx.z / parts) * parts;
   const int TB = p.block_len, G = p.G;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const float sl2 = p.scale_log2;
@@ -152,11 +156,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tok = blk * TB + t;
   // the next kernel may set itself up now; it waits for this one to complete
   grid_dep_launch();
-  // ---- row metadata of this CTA's merge half, from the (static) plan: warps
+  // ---- row metadata of this CTA's merge rows, from the (static) plan: warps
   // 4-5, idle during the level-2 attention, so the lookups overlap it ----
-  if (warp == 4 || warp == 5) {
+  if ((warp == 4 || warp == 5) && threadIdx.x - 128 < RP) {
     const int lr = threadIdx.x - 128;
-    const int Rm = rt * 128 + 64 * half + lr;
+    const int Rm = rt * 128 + RP * part + lr;
     const int tm = Rm / G, gm = Rm - (Rm / G) * G;
     const bool vm = tm < TB;
     const int tokm = blk * TB + tm;
@@ -283,10 +287,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---- phase 1b: rows of this CTA's merge half: local O -> smem, metadata ----
-  if (warp / 2 == half) {  // warps 2*half, 2*half+1 own TMEM lanes [64*half, 64*half+64)
-    const int lr = row - 64 * half;
-    meta[lr].lse_local = (p.has_local && ok) ? lse_l : -INFINITY;
+  // ---- phase 1b: this CTA's merge rows: local O -> smem ----
+  // warp w (< 4) owns TMEM lanes [32w, 32w + 32); it takes part if those lanes
+  // meet the CTA's rows [RP*part, RP*part + RP)
+  if (warp < 4 && warp * 32 < RP * (part + 1) && warp * 32 + 32 > RP * part) {
+    const int lr = row - RP * part;
+    const bool mine = lr >= 0 && lr < RP;
+    if (mine) meta[lr].lse_local = (p.has_local && ok) ? lse_l : -INFINITY;
     if (p.has_local) {
       const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
       const float sc = ok ? inv_l : 0.f;
@@ -294,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld32_wait(lane_base + 128 + c * 32, o);
+        if (!mine) continue;
         float4* dst = reinterpret_cast<float4*>(stage + lr * SP + c * 32);
 #pragma unroll
         for (int e = 0; e < 8; ++e)
@@ -311,52 +319,74 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (p.has_local && threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
 
-  // ---- phase 2: merge. A warp merges 4 rows at once, 8 lanes per row and
-  // D/8 columns per lane, so that all loads of its rows (every slot LSE and
-  // slot row) are in flight together: one memory round trip per row group ----
+  // ---- phase 2: merge. The CTA's 64 lane groups of 8 lanes (4 per warp) are
+  // spread over its RP rows, GS = 64 / RP groups per row (in the same warp); a
+  // group takes every GS-th slot of its row, 8 lanes across the row's columns
+  // (D/8 each), with up to 8 slot rows and all their LSEs in flight before any
+  // use; the row's groups then add their partial sums with shuffles ----
   // the partial slots come from the previous kernel (kernel (a)): wait for it.
   // Phase 1 reads only q and the block's K/V, which precede kernel (a).
   grid_dep_wait();
   constexpr int CPL = D / 8;          // columns per lane
   constexpr int VEC = CPL * 2 / 16;   // 16-byte vectors per lane and slot row
   constexpr int kBatch = 8;           // slot rows in flight per lane
-  static_assert(kThreads / 32 * 4 == 64, "16 warps x 4 rows");
+  constexpr int kLseBlocks = 4;       // LSE blocks of 8 slots loaded together
+  static_assert(kThreads / 32 * 4 == 64, "16 warps x 4 lane groups");
+  const int GS = 64 / RP;             // lane groups per row: 1, 2 or 4
   const int64_t sbytes = slot_bytes(D);
-  const uint8_t* part = static_cast<const uint8_t*>(p.partial);
-  const int sub = lane >> 3, j8 = lane & 7;  // row of the warp, lane within the row
-  const int lr = warp * 4 + sub;
+  const uint8_t* part_base = static_cast<const uint8_t*>(p.partial);
+  const int gi = warp * 4 + (lane >> 3), j8 = lane & 7;
+  const int lr = gi / GS, sg = gi - (gi / GS) * GS;  // row, slot group of the row
   const RowMeta mt = meta[lr];
   const bool live = mt.tok >= 0;
   const int nslots = live ? mt.nslots : 0;
-  // max over the row's 8 lanes (xor 1, 2, 4 stays inside the group)
-  auto gmax = [](float v) {
+  // the group's slots: sg, sg + GS, ...; k-th of them
+  const int nmine = nslots > sg ? (nslots - sg + GS - 1) / GS : 0;
+  // loops that shuffle run the warp's largest count (rows of a warp may map to
+  // different query tiles, e.g. with a shared trunk); lanes past their own
+  // count are predicated off
+  const int nmine_w = __reduce_max_sync(0xffffffffu, nmine);
+  auto gmax = [GS](float v) {  // max over the row's lanes
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (GS > 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+    if (GS > 2) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
     return v;
   };
-  auto gsum = [](float v) {
+  auto gsum8 = [](float v) {  // sum over the group's 8 lanes
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
   };
-  const uint8_t* prow_base = part ? part + static_cast<int64_t>(mt.prow) * D * 2 + j8 * CPL * 2
-                                  : nullptr;
-  auto slot_lse = [&](int j) -> float {
-    return *reinterpret_cast<const float*>(part + (mt.slot + j) * sbytes + kTileRows * D * 2 +
+  auto rsum = [GS](float v) {  // sum over the row's groups (same lane in each)
+    if (GS > 1) v += __shfl_xor_sync(0xffffffffu, v, 8);
+    if (GS > 2) v += __shfl_xor_sync(0xffffffffu, v, 16);
+    return v;
+  };
+  const uint8_t* prow_base =
+      part_base ? part_base + static_cast<int64_t>(mt.prow) * D * 2 + j8 * CPL * 2 : nullptr;
+  auto slot_of = [&](int k) { return mt.slot + sg + GS * k; };
+  auto slot_lse = [&](int k) -> float {
+    return *reinterpret_cast<const float*>(part_base + slot_of(k) * sbytes + kTileRows * D * 2 +
                                            mt.prow * 4);
   };
-  // first batch: slot LSEs (lane j8 holds slot j8) and the lane's part of up
-  // to kBatch slot rows, all issued before any use
-  float ls = (j8 < nslots) ? slot_lse(j8) : -INFINITY;
-  uint4 v[kBatch][VEC];
+  auto load_batch = [&](int k0, uint4 (&r)[kBatch][VEC]) {
 #pragma unroll
-  for (int j = 0; j < kBatch; ++j) {
-    if (j < nslots) {
+    for (int j = 0; j < kBatch; ++j) {
+      if (k0 + j < nmine) {
 #pragma unroll
-      for (int c = 0; c < VEC; ++c)
-        v[j][c] = reinterpret_cast<const uint4*>(prow_base + (mt.slot + j) * sbytes)[c];
+        for (int c = 0; c < VEC; ++c)
+          r[j][c] = reinterpret_cast<const uint4*>(prow_base + slot_of(k0 + j) * sbytes)[c];
+      }
     }
-  }
+  };
+  // first batch of slot rows and the LSEs of up to 8 * kLseBlocks slots of the
+  // group (lane j8 holds the LSE of the group's slot j8 + 8b), all in flight
+  uint4 v[kBatch][VEC];
+  load_batch(0, v);
+  float ls[kLseBlocks];
+#pragma unroll
+  for (int b = 0; b < kLseBlocks; ++b) ls[b] = (8 * b + j8 < nmine) ? slot_lse(8 * b + j8) : -INFINITY;
   // dense prefix state (no partial slots)
   float lse_p = -INFINITY;
   const T* po = nullptr;
@@ -366,31 +396,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     lse_p = p.prefix_lse[static_cast<int64_t>(mt.tok) * p.pl_st + mt.hq];
   }
   const float lse_local = live ? mt.lse_local : -INFINITY;
-  float M = fmaxf(lse_local, lse_p);
-  M = fmaxf(M, gmax(ls));
-  for (int s0 = 8; s0 < nslots; s0 += 8)  // more than 8 slots: rare
-    M = fmaxf(M, gmax(s0 + j8 < nslots ? slot_lse(s0 + j8) : -INFINITY));
+  float lmax = -INFINITY;
+#pragma unroll
+  for (int b = 0; b < kLseBlocks; ++b) lmax = fmaxf(lmax, ls[b]);
+  for (int k0 = 8 * kLseBlocks; k0 < nmine_w; k0 += 8)  // very many slots
+    lmax = fmaxf(lmax, k0 + j8 < nmine ? slot_lse(k0 + j8) : -INFINITY);
+  const float M = fmaxf(fmaxf(lse_local, lse_p), gmax(lmax));
   const float Mz = (M == -INFINITY) ? 0.f : M;
   const float w_l = (lse_local == -INFINITY) ? 0.f : fast_exp2(lse_local - Mz);
   const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
   float acc[CPL];
-  if (p.has_local && live) {
-    const float4* st = reinterpret_cast<const float4*>(stage + lr * SP + j8 * CPL);
 #pragma unroll
-    for (int e = 0; e < CPL / 4; ++e) {
-      const float4 x = st[e];
-      acc[4 * e] = w_l * x.x;
-      acc[4 * e + 1] = w_l * x.y;
-      acc[4 * e + 2] = w_l * x.z;
-      acc[4 * e + 3] = w_l * x.w;
+  for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
+  if (sg == 0) {  // the local and dense-prefix states enter once per row
+    if (p.has_local && live) {
+      const float4* st = reinterpret_cast<const float4*>(stage + lr * SP + j8 * CPL);
+#pragma unroll
+      for (int e = 0; e < CPL / 4; ++e) {
+        const float4 x = st[e];
+        acc[4 * e] = w_l * x.x;
+        acc[4 * e + 1] = w_l * x.y;
+        acc[4 * e + 2] = w_l * x.z;
+        acc[4 * e + 3] = w_l * x.w;
+      }
     }
-  } else {
+    if (po) {
 #pragma unroll
-    for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
-  }
-  if (po) {
-#pragma unroll
-    for (int e = 0; e < CPL; ++e) acc[e] = fmaf(w_p, Num<T>::to_f(po[e]), acc[e]);
+      for (int e = 0; e < CPL; ++e) acc[e] = fmaf(w_p, Num<T>::to_f(po[e]), acc[e]);
+    }
   }
   auto add_row = [&](float wj, const uint4 (&r)[VEC]) {
 #pragma unroll
@@ -403,29 +436,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   };
-  float w = (ls == -INFINITY) ? 0.f : fast_exp2(ls - Mz);  // weight of slot j8
-  float den = w_l + w_p + gsum(w);
+  float den = 0.f;
+  for (int k0 = 0; k0 < nmine_w; k0 += kBatch) {
+    if (k0 > 0) load_batch(k0, v);  // later batches: 8 rows in flight again
+    const int b = k0 / 8;
+    float l = -INFINITY;
+    if (b < kLseBlocks) {
 #pragma unroll
-  for (int j = 0; j < kBatch; ++j) {
-    const float wj = __shfl_sync(0xffffffffu, w, (lane & ~7) + j);
-    if (j < nslots) add_row(wj, v[j]);
-  }
-  for (int s0 = kBatch; s0 < nslots; s0 += 8) {  // more than 8 slots: rare
-    const float l2 = s0 + j8 < nslots ? slot_lse(s0 + j8) : -INFINITY;
-    const float w2 = (l2 == -INFINITY) ? 0.f : fast_exp2(l2 - Mz);
-    den += gsum(w2);
-    for (int j = 0; j < 8; ++j) {
-      const float wj = __shfl_sync(0xffffffffu, w2, (lane & ~7) + j);
-      if (s0 + j < nslots) {
-        uint4 r[VEC];
+      for (int q = 0; q < kLseBlocks; ++q)
+        if (q == b) l = ls[q];
+    } else if (k0 + j8 < nmine) {
+      l = slot_lse(k0 + j8);
+    }
+    const float w = (l == -INFINITY) ? 0.f : fast_exp2(l - Mz);  // weight of slot k0 + j8
+    den += gsum8(w);
 #pragma unroll
-        for (int c = 0; c < VEC; ++c)
-          r[c] = reinterpret_cast<const uint4*>(prow_base + (mt.slot + s0 + j) * sbytes)[c];
-        add_row(wj, r);
-      }
+    for (int j = 0; j < kBatch; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w, (lane & ~7) + j);
+      if (k0 + j < nmine) add_row(wj, v[j]);
     }
   }
-  if (live) {
+  // the row's groups add up: acc, den over groups (the local/prefix weights once)
+#pragma unroll
+  for (int e = 0; e < CPL; ++e) acc[e] = rsum(acc[e]);
+  den = rsum(den) + w_l + w_p;
+  if (live && sg == 0) {
     const float lse_out = den > 0.f ? Mz + fast_log2(den) : -INFINITY;
     float factor = den > 0.f ? 1.f / den : 0.f;
     if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
@@ -559,6 +594,17 @@ __global__ void merge_state_kernel(T* v, int64_t v_st, int64_t v_sh, float* s, i
 
 namespace d2sd {
 namespace {
+// Merge parts per 128-row tile (64, 32 or 16 rows per CTA): more CTAs, and
+// more lanes per row, when few tiles would leave most SMs idle (KV-head
+// sharding over several GPUs leaves each with few heads, and each query tile
+// then has many partial slots to merge).
+int merge_parts(int64_t tiles) {
+  const int64_t sms = current_sm_count();
+  int parts = 2;
+  while (parts < 8 && tiles * parts * 2 <= sms) parts *= 2;
+  return parts;
+}
+
 struct PeerArgs {
   void* const* out_ptrs = nullptr;
   unsigned long long* const* counters = nullptr;
@@ -676,12 +722,18 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
       rc = encode_tensor_map(&tv, tdt, v_local, 3, dims, str, box, "v_local");
       if (rc) return rc;
     }
-    grid = dim3(num_blocks, num_kv_heads, 2 * ((block_len * G + 127) / 128));
+    const int64_t base = static_cast<int64_t>(num_blocks) * num_kv_heads * ((block_len * G + 127) / 128);
+    const int parts = merge_parts(base);
+    prm.rows_per_cta = plan::kTileRows / parts;
+    grid = dim3(num_blocks, num_kv_heads, static_cast<unsigned>(parts * ((block_len * G + 127) / 128)));
   } else {
     // no level 2: the blocks do not matter, tile all tokens of a head together
     const int64_t ntok = static_cast<int64_t>(num_blocks) * block_len;
     prm.block_len = static_cast<int32_t>(ntok);
-    grid = dim3(1, num_kv_heads, static_cast<unsigned>(2 * ((ntok * G + 127) / 128)));
+    const int64_t tiles = (ntok * G + 127) / 128;
+    const int parts = merge_parts(static_cast<int64_t>(num_kv_heads) * tiles);
+    prm.rows_per_cta = plan::kTileRows / parts;
+    grid = dim3(1, num_kv_heads, static_cast<unsigned>(parts * tiles));
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == D2SD_DTYPE_BF16) return dispatch_suffix<__nv_bfloat16>(tq, tk, tv, prm, head_dim, NK, grid, st);

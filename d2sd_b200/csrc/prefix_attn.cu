@@ -101,18 +101,12 @@ struct PrefixParams {
 __device__ __forceinline__ uint32_t s_col(int i) { return static_cast<uint32_t>(i * 128); }
 __device__ __forceinline__ uint32_t o_col(int i) { return static_cast<uint32_t>(256 + i * 128); }
 
-// Warp-uniform bounded wait: lane 0 polls, the verdict is broadcast.
+// Warp-uniform bounded wait: every lane polls the barrier itself (one warp-wide
+// try_wait per poll), which notices a completed phase sooner than one lane
+// polling and broadcasting; the warp goes on only if every lane saw it.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (ok) {
-    // the phase has completed and cannot advance without this warp, so every
-    // lane's own acquire of it succeeds at once
-    while (!mbar_try_wait(bar, parity)) {
-    }
-  }
-  return ok != 0;
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Producer warp. The page indices of a KV tile are fetched by the whole warp
@@ -242,35 +236,48 @@ __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const
 
 // K in smem: row layout = two 128-byte-swizzled panels of 64 columns; native
 // layout = pages of [2 row groups][D/8 chunks][8 rows][16 B] (no swizzle).
+// The MMA issuer is one thread whose instruction latencies are all exposed, and
+// the tensor core runs ahead of it by little more than one MMA: any work between
+// two MMAs of a block idles the tensor pipe. So every descriptor is built once
+// and moved with an immediate: the start-address field is the low 14 bits
+// (address >> 4) and shared addresses are below 256 KB, so moving a descriptor
+// by b bytes adds b >> 4 to its low word without a carry out of the field.
+__device__ __forceinline__ uint64_t desc_at(uint64_t d, uint32_t bytes) {
+  uint32_t lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(d));
+  lo += bytes >> 4;
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+
+// S_i = Q_i K^T: M=128, N=128 keys, K = D in steps of 16. qd: descriptor of
+// Q tile i; kd: descriptor of the K stage. Q and row-layout K are two
+// 128-byte-swizzled panels of 64 columns (kPanelBytes apart); native K is pages
+// of [2 row groups][D/8 chunks][8 rows][16 B] (16-byte chunks 128 B apart).
 template <int D, bool NATIVE>
-__device__ __forceinline__ void issue_qk(uint32_t tmem, int i, uint8_t* smem, int stage) {
-  using C = Cfg<D>;
+__device__ __forceinline__ void issue_qk(uint32_t tmem_s, uint64_t qd, uint64_t kd) {
   constexpr uint32_t idesc = umma_idesc_bf16(128, 128, false);
-  constexpr uint32_t kGroup = (D / 8) * 128;  // native: bytes per 8-row group
-  const uint32_t a0 = smem_u32(smem + C::kSmemQ + i * C::kTileBytes);
-  const uint32_t b0 = smem_u32(smem + C::kSmemK + stage * C::kTileBytes);
 #pragma unroll
   for (int ks = 0; ks < D / 16; ++ks) {
     const uint32_t off = (ks / 4) * kPanelBytes + (ks % 4) * 32;
-    const uint64_t bdesc = NATIVE ? umma_desc_noswz(b0 + ks * 256, 128, kGroup)
-                                  : umma_desc_sw128(b0 + off, 16, 1024);
-    umma_ss(tmem + s_col(i), umma_desc_sw128(a0 + off, 16, 1024), bdesc, idesc, ks > 0 ? 1u : 0u);
+    umma_ss(tmem_s, desc_at(qd, off), desc_at(kd, NATIVE ? ks * 256 : off), idesc,
+            ks > 0 ? 1u : 0u);
   }
 }
 
+// O_i (+)= P_i V for the 16-key steps [KS0, KS1): A = P (packed bf16 in the
+// first 64 columns of S_i), B = V (MN-major). vd: descriptor of the V stage;
+// native V: one page (16 keys = 2 groups of kGroup bytes) per step; row V: 16
+// rows of 128 B per step in each 64-column panel.
 template <int D, bool NATIVE, int KS0, int KS1>
-__device__ __forceinline__ void issue_pv(uint32_t tmem, int i, uint8_t* smem, int stage,
+__device__ __forceinline__ void issue_pv(uint32_t tmem_o, uint32_t tmem_p, uint64_t vd,
                                          bool accumulate) {
-  using C = Cfg<D>;
   constexpr uint32_t idesc = umma_idesc_bf16(128, D, true);
-  constexpr uint32_t kGroup = (D / 8) * 128;  // native: bytes per 8-key group
-  const uint32_t b0 = smem_u32(smem + C::kSmemV + stage * C::kTileBytes);
+  constexpr uint32_t kGroup = (D / 8) * 128;
 #pragma unroll
   for (int ks = KS0; ks < KS1; ++ks) {
-    // native: one page (16 keys = 2 groups) per K step; MN chunks 16 B apart
-    const uint64_t bdesc = NATIVE ? umma_desc_noswz(b0 + ks * 2 * kGroup, kGroup, 128)
-                                  : umma_desc_sw128(b0 + ks * 16 * 128, kPanelBytes, 1024);
-    umma_ts(tmem + o_col(i), tmem + s_col(i) + ks * 8, bdesc, idesc,
+    umma_ts(tmem_o, tmem_p + ks * 8, desc_at(vd, NATIVE ? ks * 2 * kGroup : ks * 16 * 128), idesc,
             (accumulate || ks > 0) ? 1u : 0u);
   }
 }
@@ -279,7 +286,16 @@ template <int D, bool NATIVE>
 __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars, uint32_t tmem,
                            volatile int* abort, int item_begin, int item_end) {
   using C = Cfg<D>;
+  constexpr uint32_t kGroup = (D / 8) * 128;
   const int32_t* items = p.plan + p.plan[H_OFF_ITEMS];
+  const uint64_t qd0 = umma_desc_sw128(smem_u32(smem + C::kSmemQ), 16, 1024);
+  const uint64_t qd1 = desc_at(qd0, C::kTileBytes);
+  const uint64_t kd0 = NATIVE ? umma_desc_noswz(smem_u32(smem + C::kSmemK), 128, kGroup)
+                              : umma_desc_sw128(smem_u32(smem + C::kSmemK), 16, 1024);
+  const uint64_t vd0 = NATIVE ? umma_desc_noswz(smem_u32(smem + C::kSmemV), kGroup, 128)
+                              : umma_desc_sw128(smem_u32(smem + C::kSmemV), kPanelBytes, 1024);
+  const uint32_t ts0 = tmem + s_col(0), ts1 = tmem + s_col(1);
+  const uint32_t to0 = tmem + o_col(0), to1 = tmem + o_col(1);
   uint32_t kt = 0;
   uint32_t pcount[2] = {0, 0};
   for (int it = item_begin; it < item_end; ++it) {
@@ -292,9 +308,10 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
       const int sk = static_cast<int>(kt % C::kKStages);
       if (!mbar_wait(&bars[C::B_KFULL + sk], (kt / C::kKStages) & 1, abort)) return;
       tc_fence_after();
-      issue_qk<D, NATIVE>(tmem, 0, smem, sk);
+      const uint64_t kd = desc_at(kd0, sk * C::kTileBytes);
+      issue_qk<D, NATIVE>(ts0, qd0, kd);
       umma_commit(&bars[C::B_SFULL + 0]);
-      issue_qk<D, NATIVE>(tmem, 1, smem, sk);
+      issue_qk<D, NATIVE>(ts1, qd1, kd);
       umma_commit(&bars[C::B_SFULL + 1]);
       umma_commit(&bars[C::B_KEMPTY + sk]);
       if (n == 1) umma_commit(&bars[C::B_QFREE]);
@@ -304,6 +321,8 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
       const int sv = static_cast<int>(cur % C::kVStages);
       const bool has_next = j + 1 < n;
       const int skn = static_cast<int>((cur + 1) % C::kKStages);
+      const uint64_t vd = desc_at(vd0, sv * C::kTileBytes);
+      const uint64_t kdn = desc_at(kd0, skn * C::kTileBytes);
       if (!mbar_wait(&bars[C::B_VFULL + sv], (cur / C::kVStages) & 1, abort)) return;
       // ---- tile 0 ----
       if (j == 0 && k > 0) {
@@ -312,15 +331,15 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
       // P.V in two halves: keys 0..63 as soon as their P is in TMEM
       if (!mbar_wait(&bars[C::B_PHALF + 0], pcount[0] & 1, abort)) return;
       tc_fence_after();
-      issue_pv<D, NATIVE, 0, 4>(tmem, 0, smem, sv, j > 0);
+      issue_pv<D, NATIVE, 0, 4>(to0, ts0, vd, j > 0);
       if (!mbar_wait(&bars[C::B_PFULL + 0], pcount[0] & 1, abort)) return;
       ++pcount[0];
       tc_fence_after();
-      issue_pv<D, NATIVE, 4, 8>(tmem, 0, smem, sv, true);
+      issue_pv<D, NATIVE, 4, 8>(to0, ts0, vd, true);
       if (has_next) {
         if (!mbar_wait(&bars[C::B_KFULL + skn], ((cur + 1) / C::kKStages) & 1, abort)) return;
         tc_fence_after();
-        issue_qk<D, NATIVE>(tmem, 0, smem, skn);
+        issue_qk<D, NATIVE>(ts0, qd0, kdn);
         umma_commit(&bars[C::B_SFULL + 0]);
       }
       // ---- tile 1 ----
@@ -329,14 +348,14 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
       }
       if (!mbar_wait(&bars[C::B_PHALF + 1], pcount[1] & 1, abort)) return;
       tc_fence_after();
-      issue_pv<D, NATIVE, 0, 4>(tmem, 1, smem, sv, j > 0);
+      issue_pv<D, NATIVE, 0, 4>(to1, ts1, vd, j > 0);
       if (!mbar_wait(&bars[C::B_PFULL + 1], pcount[1] & 1, abort)) return;
       ++pcount[1];
       tc_fence_after();
-      issue_pv<D, NATIVE, 4, 8>(tmem, 1, smem, sv, true);
+      issue_pv<D, NATIVE, 4, 8>(to1, ts1, vd, true);
       umma_commit(&bars[C::B_VEMPTY + sv]);
       if (has_next) {
-        issue_qk<D, NATIVE>(tmem, 1, smem, skn);
+        issue_qk<D, NATIVE>(ts1, qd1, kdn);
         umma_commit(&bars[C::B_SFULL + 1]);
         umma_commit(&bars[C::B_KEMPTY + skn]);
         if (j + 2 == n) umma_commit(&bars[C::B_QFREE]);

@@ -489,9 +489,12 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
           release_half(c);
         }
       }
-      if (f != 1.f) {
-        // O holds the sum up to the previous tile: this tile's S commit follows
-        // the previous P.V in issue order, so that P.V has completed
+      if (!early) {
+        // some lane of this warp rescales O. The TMEM loads and stores are
+        // warp-collective (.sync.aligned), so the whole warp runs them, lanes
+        // with f = 1 unchanged. O holds the sum up to the previous tile: this
+        // tile's S commit follows the previous P.V in issue order, so that P.V
+        // has completed
         l_run *= f;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {

@@ -51,6 +51,26 @@ def test_single_prefill_contiguous(cuda_device, N, P, Hq, Hk, D, layout):
     close(lse, rl, atol=LSE_ATOL)
 
 
+@pytest.mark.parametrize("D", [128, 64])
+def test_single_prefill_growing_scores(cuda_device, D):
+    """Keys whose scale steps up every 192 keys, so that the rows' running max
+    is overtaken by more than 8 (log2 units) inside items, in the first half of
+    some 128-key tiles and in the second half of others: the rescale paths of
+    kernel (a) run beside its fast path on the same launch."""
+    import d2sd_b200 as d
+    N, P, Hq, Hk = 256, 4096, 8, 2
+    g = torch.Generator().manual_seed(77 + D)
+    q = rand((N, Hq, D), g, cuda_device)
+    ramp = (1.0 + 4.0 * (torch.arange(P) // 192)).view(P, 1, 1)
+    k = (torch.randn((P, Hk, D), generator=g) * ramp).to(torch.bfloat16).to(cuda_device)
+    v = rand((P, Hk, D), g, cuda_device)
+    out, lse = d.single_prefill_with_kv_cache(q, k, v, causal=False, return_lse=True,
+                                              sm_scale=D ** -0.5)
+    ro, rl = AT.single_prefill(f64(q), f64(k), f64(v), causal=False, sm_scale=D ** -0.5)
+    close(out, ro)
+    close(lse, rl, atol=LSE_ATOL)
+
+
 @pytest.mark.parametrize("layout", ["umma", "hnd"])
 @pytest.mark.parametrize("page_order", ["identity", "shuffled"])
 @pytest.mark.parametrize("P,window", [(2048, None), (777, None), (1000, 128), (130, 128)])

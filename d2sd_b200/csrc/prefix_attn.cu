@@ -62,7 +62,9 @@ struct Cfg {
   static constexpr int kSmemQ = 0;
   static constexpr int kSmemK = kSmemQ + 2 * kTileBytes;
   static constexpr int kSmemV = kSmemK + kKStages * kTileBytes;
-  static constexpr int kSmemBar = kSmemV + kVStages * kTileBytes;
+  // epilogue staging: 4 KB per softmax warp (32 rows x 128 bytes of O)
+  static constexpr int kSmemStage = kSmemV + kVStages * kTileBytes;
+  static constexpr int kSmemBar = kSmemStage + 8 * 4096;
   // barrier indices
   static constexpr int B_QFULL = 0;
   static constexpr int B_QFREE = 1;
@@ -368,7 +370,8 @@ __device__ void mma_issuer(const PrefixParams& p, uint8_t* smem, uint64_t* bars,
 }
 
 template <int D>
-__device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tmem, volatile int* abort,
+__device__ void softmax_role(const PrefixParams& p, uint8_t* smem, uint64_t* bars, uint32_t tmem,
+                             volatile int* abort,
                              int item_begin, int item_end) {
   using C = Cfg<D>;
   const int i = threadIdx.x / 128;         // query tile of this warpgroup
@@ -523,20 +526,38 @@ __device__ void softmax_role(const PrefixParams& p, uint64_t* bars, uint32_t tme
       // merge), base-2 LSE in fp32
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       uint8_t* sb = reinterpret_cast<uint8_t*>(p.partial) + static_cast<int64_t>(slot) * slot_bytes(D);
-      uint4* dst = reinterpret_cast<uint4*>(sb + static_cast<int64_t>(row) * D * 2);
+      // Each thread holds its own row; storing it directly would scatter every
+      // warp store over 32 rows. So each 64-column panel goes through this
+      // warp's 4 KB of shared memory (32 rows x 128 B, 16-byte chunk c of row
+      // r at chunk c ^ (r & 7): conflict-free both ways) and leaves as four
+      // whole 128-byte row segments per store instruction.
+      uint8_t* stg = smem + C::kSmemStage + (threadIdx.x / 32) * 4096;
+      uint8_t* gw = sb + static_cast<int64_t>(wq * 32) * D * 2;  // this warp's 32 rows
+#pragma unroll 1
+      for (int pn = 0; pn < D / 64; ++pn) {
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32_wait(lane_base + o_col(i) + c * 32, o);
+        for (int hc = 0; hc < 2; ++hc) {
+          uint32_t o[32];
+          tmem_ld32_wait(lane_base + o_col(i) + pn * 64 + hc * 32, o);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          uint4 v;
-          v.x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv);
-          v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv);
-          v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv);
-          v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv);
-          dst[c * 4 + e] = v;
+          for (int e = 0; e < 4; ++e) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * e + 0]) * inv, __uint_as_float(o[8 * e + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * e + 2]) * inv, __uint_as_float(o[8 * e + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * e + 4]) * inv, __uint_as_float(o[8 * e + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * e + 6]) * inv, __uint_as_float(o[8 * e + 7]) * inv);
+            const int c = hc * 4 + e;
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = v;
+          }
         }
+        __syncwarp();
+#pragma unroll
+        for (int k4 = 0; k4 < 8; ++k4) {
+          const int r = 4 * k4 + (lane >> 3), c = lane & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+          *reinterpret_cast<uint4*>(gw + static_cast<int64_t>(r) * D * 2 + pn * 128 + c * 16) = v;
+        }
+        __syncwarp();
       }
       const float lse = l_run > 0.f ? m_run + fast_log2(l_run) : -INFINITY;
       reinterpret_cast<float*>(sb + static_cast<int64_t>(kTileRows) * D * 2)[row] = lse;
@@ -616,7 +637,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
-    softmax_role<D>(p, bars, tmem, abort, item_begin, item_end);
+    softmax_role<D>(p, smem, bars, tmem, abort, item_begin, item_end);
   }
 
   tc_fence_before();

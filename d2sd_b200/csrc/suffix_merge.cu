@@ -8,9 +8,10 @@
 // tokens, then merge_state_in_place into the level-1 state; the sink rescale
 // out *= sigmoid(lse - sink) follows at generation/verification.py:173-176.
 //
-// One launch covers every branch. A CTA owns (block, kv head, 128-row tile);
-// rows are token*G + g, the G query heads of the kv head, so the whole GQA
-// group shares one K/V tile. Thread 0 TMA-loads the Q tile and the block's K
+// One launch covers every branch. 2, 4 or 8 CTAs share each (block, kv head,
+// 128-row tile); each computes the tile's level-2 attention and merges 64, 32
+// or 16 of its rows. Rows are token*G + g, the G query heads of the kv head, so
+// the whole GQA group shares one K/V tile. Thread 0 TMA-loads the Q tile and the block's K
 // and V (128-byte swizzle) and issues S = Q K^T on tcgen05 into TMEM
 // (M=128, N=32 or 64 keys); each thread (= TMEM lane = row) masks (causal,
 // full or a custom bitmask), exponentiates and writes P back to TMEM as

@@ -77,6 +77,12 @@ def decode(plan):
          Hq=32, Hk=8, sms=148),                                     # batched serving
     dict(q=[96], kv=[(16384 - 128, 16384)], Hq=64, Hk=8, sms=148),   # GPT-OSS sliding layer
     dict(q=[96], kv=[(0, 16384)], Hq=64, Hk=8, sms=148),            # GPT-OSS full layer
+    # one rank's share under KV-head sharding: north star on 2, 4 and 8 GPUs,
+    # GPT-OSS full layer on 8
+    dict(q=[256], kv=[(0, 32768)], Hq=16, Hk=4, sms=148),
+    dict(q=[256], kv=[(0, 32768)], Hq=8, Hk=2, sms=148),
+    dict(q=[256], kv=[(0, 32768)], Hq=4, Hk=1, sms=148),
+    dict(q=[96], kv=[(0, 16384)], Hq=8, Hk=1, sms=148),
     dict(q=[64, 3, 0, 17], kv=[(0, 5), (0, 0), (0, 100), (7, 300)], Hq=8, Hk=2, sms=10),
     dict(q=[64], kv=[(0, 512)], Hq=32, Hk=8, sms=1),
 ])

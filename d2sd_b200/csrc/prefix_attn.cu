@@ -26,7 +26,9 @@
 // TMEM: S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [384,384+D); P_i is written
 // as packed bf16 over the first 64 columns of S_i.
 // The two tiles ping-pong: while warpgroup 0 turns S0 into P0 the tensor core
-// runs Q1 K^T and P1 V, and vice versa.
+// runs Q1 K^T and P1 V, and vice versa. At the end of an item each softmax warp
+// normalises its 32 rows of O to bf16 and writes them to the item's partial
+// slot through 4 KB of shared memory, so the stores are whole row segments.
 #include "common.cuh"
 #include "plan_layout.h"
 
@@ -111,11 +113,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
-// Producer warp. The page indices of a KV tile are fetched by the whole warp
-// (lane b reads page b of the tile) one tile ahead of their use, so no copy
-// waits on a dependent page-table load. Row-layout caches go through TMA tensor
-// boxes issued by lane 0; UMMA-native pages are one bulk copy per page per
-// operand, lane b copying page b.
 // 2^x for a pair of x <= 8 on the FMA pipe, to take part of the exponentials
 // off the ex2 pipe (16 lanes per clock per SM on sm_100, half the softmax's
 // time). Cody-Waite style reduction: x = j + f with j = round(x) through the
@@ -142,9 +139,14 @@ __device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
 }
 
 // pairs of each 32-key chunk whose exponentials go to exp2_poly2 (bit e = pair
-// e): one in eight, measured best on cfg3 (one in four was no better)
+// e): one in eight, measured best on cfg3 (one in four to one in two was slower)
 constexpr uint32_t kPolyPairs = 0x8080u;
 
+// Producer warp. The page indices of a KV tile are fetched by the whole warp
+// (lane b reads page b of the tile) one tile ahead of their use, so no copy
+// waits on a dependent page-table load. Row-layout caches go through TMA tensor
+// boxes issued by lane 0; UMMA-native pages are one bulk copy per page per
+// operand, lane b copying page b.
 template <int D, bool NATIVE>
 __device__ void producer(const CUtensorMap* tm_q, const CUtensorMap* tm_k, const CUtensorMap* tm_v,
                          const PrefixParams& p, uint8_t* smem, uint64_t* bars, volatile int* abort,

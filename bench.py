@@ -311,6 +311,8 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
             e.record(stream)
             ev[name].append(e)
 
+    bstatus = torch.zeros(1, dtype=torch.int32, device=dev)  # kernel (b)'s wait time-outs
+
     def step(qs, kns, vns, lg, bid, timing=False, wait_layer=None, wait_logits=None):
         for l in range(L):
             if wait_layer is not None:
@@ -324,7 +326,7 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
             ops.suffix_merge(qs_full[l], kns[l].reshape(N, hk, D), vns[l].reshape(N, hk, D), out,
                              lse, num_blocks=B, block_len=T, num_qo_heads=hq, num_kv_heads=hk,
                              sm_scale=scale, partial=plan.partial, plan_dev=plan.plan,
-                             prefix_token=ptok, exchange=px)
+                             prefix_token=ptok, exchange=px, status=bstatus)
             if timing:
                 mark("b1")
             if gathered is not None:
@@ -364,22 +366,26 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
     sampler.start()
     time.sleep(0.3)
     ev = {k: [] for k in ("a0", "a1", "b1", "c0", "c1", "d1")}
+    if px is not None:
+        px.reset_stats()
     barrier()
     t_begin = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_begin.record(stream)
     for i in range(a.steps):
-        # per-kernel events on the last step only: an event between two kernels
-        # keeps the second from starting early (the programmatic launch overlap),
-        # so a marked step runs about 1.5 ms slower; the other steps run as a
-        # caller's would. The last step still gives one event pair per launch of
-        # (a) and (b) for every layer.
-        step(q_pref, kns, vns, logits, ids, timing=(i == a.steps - 1))
+        step(q_pref, kns, vns, logits, ids)
     t_end.record(stream)
     barrier()
     clocks = sampler.stop()
     ms_total = max_over_ranks(t_begin.elapsed_time(t_end))
     ms_step = ms_total / a.steps
+    xwait = px.wait_stats() if px is not None else None
+    # per-kernel events on one extra step after the timed region: an event
+    # between two kernels keeps the second from starting early (the programmatic
+    # launch overlap), so a marked step runs slower than the timed ones; it
+    # gives one event pair per launch of (a) and (b) for every layer
+    step(q_pref, kns, vns, logits, ids, timing=True)
+    barrier()
     a_ms = [s.elapsed_time(e) for s, e in zip(ev["a0"], ev["a1"])]
     b_ms = [s.elapsed_time(e) for s, e in zip(ev["a1"], ev["b1"])]
     c_ms = [s.elapsed_time(e) for s, e in zip(ev["c0"], ev["c1"])]
@@ -423,6 +429,13 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
     a_b2b = loop_ms(run_a)
     ab_b2b = loop_ms(run_ab)
     value = N * a.steps / (ms_total / 1e3)
+    # no line from a run in which any kernel gave up a bounded wait
+    statuses = {"a": int(plan.status.item()), "b": int(bstatus.item())}
+    if px is not None:
+        statuses["exchange"] = int(px.status.item())
+    bad = {k: v for k, v in statuses.items() if v}
+    if bad:
+        raise SystemExit(f"rank {rank}: kernel status words nonzero {bad}: no bench line")
 
     # --- end to end: host buffers, copies inside the timed region --------------
     e2e = None
@@ -502,13 +515,15 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
     traffic = profile_traffic("prefix_attention_cfg3.txt") if (world == 1 and P == 32768 and
                                                                 not a.shared) else None
     achieved_b2b = flops_a / (a_b2b / 1e3) / 1e12
-    roofline = {"bound": "tensor", "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s",
-                "frac": achieved / tf_sust, "traffic": traffic,
-                "achieved_back_to_back": achieved_b2b, "frac_back_to_back": achieved_b2b / tf_sust,
-                "timing": ("achieved: per-launch CUDA events on the last step of the timed region "
-                           "(each includes its launch latency); back_to_back: kernel (a) alone "
-                           "over all layers, events around the loop only"),
-                "peak_source": f"bf16_tflops_sustained of {peak_src} (kernel timed inside a long step)",
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
+                "frac": achieved / tf_burst, "traffic": traffic,
+                "achieved_back_to_back": achieved_b2b, "frac_back_to_back": achieved_b2b / tf_burst,
+                "frac_of_sustained": achieved / tf_sust,
+                "timing": ("achieved: per-launch CUDA events on a marked step after the timed "
+                           "region (each includes its launch latency); back_to_back: kernel (a) "
+                           "alone over all layers, events around the loop only"),
+                "peak_source": (f"bf16_tflops (burst) of {peak_src}: the timed region lasts "
+                                f"{ms_total / 1e3:.2f} s at full clock"),
                 "kernel": "prefix_attention_kernel (a)",
                 "algorithmic": f"4*N_u*Hq*P*D = {flops_a:.4g} FLOP per launch"}
     bytes_c = B * T * V * 2 + B * T * 8
@@ -530,7 +545,7 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
         "hbm_peak_gbs": hbm,
         "hbm_frac": {"b": gbs(bytes_b, b_avg) / hbm, "c": gbs(bytes_c, c_avg) / hbm,
                      "d": gbs(bytes_d, d_avg) / hbm},
-        "attention_us_per_layer": (a_avg + b_avg) * 1e3,
+        "attention_us_per_layer_marked": (a_avg + b_avg) * 1e3,
         "a_back_to_back_us": a_b2b * 1e3,
         "b_marginal_back_to_back_us": (ab_b2b - a_b2b) * 1e3,
         "acceptance_length": acc_len,
@@ -540,10 +555,18 @@ def run_d2sd(a, rank: int, world: int, local_rank: int):
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) Q/K/V and logits; drafts match argmax w.p. 0.7)",
-        "config": workload_config(a, world), "us_per_layer": (a_avg + b_avg) * 1e3,
+        "config": workload_config(a, world),
+        "us_per_layer": (ms_step - c_avg - d_avg) / L * 1e3,
+        "status": statuses,
         "roofline": roofline, "kernels": kernels, "clocks": clocks, "e2e": e2e,
         "gpu_launches": a.steps * (2 * L + 2),
     }
+    if xwait is not None:
+        # time the signalling CTA of kernel (b) waited for the other ranks, per
+        # layer, in the timed region (the worst rank's mean and maximum)
+        line["exchange_wait"] = {"mean_us_per_layer": max_over_ranks(xwait["mean_wait_us"]),
+                                 "max_us": max_over_ranks(xwait["max_wait_us"]),
+                                 "waits": xwait["waits"]}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cb = cpu_sample(a)
         cb.pop("seconds_per_step", None)

@@ -7,7 +7,11 @@ Public surface (mirrors the reference's call surface):
   cascade_attention, CascadePlan, Request
                                 plan/run form of the two-level verify attention
   verify, Verifier              greedy acceptance (generation/d3_generator.py:204-225)
+  BatchVerifier                 the same for a batch of requests in one launch
+  ShardedVerifier               vocabulary-sharded acceptance across GPUs (NVLink
+                                exchange of the rows' bests inside the kernel)
   PagedKVCache                  paged target cache with the accepted-branch commit
+  PagedKVPool                   many sequences in one page pool, batched commit
   cascade_verify_forward        generation/verification.py:cascade_verify_forward
                                 on these kernels
   PeerExchange                  KV-head-sharded output all-gather done by kernel (b)'s
@@ -16,19 +20,23 @@ Public surface (mirrors the reference's call surface):
 All compute runs in ``libd2sd.so`` (built by ``python -m d2sd_b200.build``);
 importing a kernel entry point without it raises.
 """
-from .accept import Verifier, verify
+from .accept import BatchVerifier, ShardedVerifier, Verifier, verify
 from .cascade import CascadePlan, Request, cascade_attention, shared_trunk_map
 from .flashinfer_compat import merge_state_in_place, single_prefill_with_kv_cache
-from .kv_cache import PagedKVCache
+from .kv_cache import PagedKVCache, PagedKVPool
 from .runner import CascadeGraphRunner
-from .sharding import PeerExchange
+from .sharding import PeerExchange, RecordExchange
 
 __all__ = [
+    "BatchVerifier",
     "CascadeGraphRunner",
     "CascadePlan",
     "PagedKVCache",
+    "PagedKVPool",
     "PeerExchange",
+    "RecordExchange",
     "Request",
+    "ShardedVerifier",
     "Verifier",
     "cascade_attention",
     "merge_state_in_place",

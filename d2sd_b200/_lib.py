@@ -66,6 +66,14 @@ SIGNATURES = {
                                  i64, vp]),
     "d2sd_verify_accept_noalloc": (i32, [vp, i32, i32, i32, i64, i64, i64, vp, i64, i64, vp,
                                          vp, vp, vp]),
+    "d2sd_verify_accept_batch_workspace_size": (i64, [i32, i32, i32, i64]),
+    "d2sd_verify_accept_batch": (i32, [vp, i32, i32, i32, i32, i64, i64, i64, i64, vp, i64, i64,
+                                       i64, vp, vp, vp, vp, i64, vp]),
+    "d2sd_verify_accept_sharded": (i32, [vp, i32, i32, i32, i32, i64, i64, i64, i64, i64, vp,
+                                         i64, i64, i64, vp, vp, vp, vp, i64, vp, vp, i32, i32,
+                                         i64, vp, vp]),
+    "d2sd_commit_kv_batch": (i32, [vp, i32, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64,
+                                   i64, i64, i32, i32, vp, vp, vp, vp, vp]),
     "d2sd_commit_kv": (i32, [vp, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64, i64, i32, i32,
                              vp, vp, vp, i64, vp]),
     "d2sd_qk_norm_rope": (i32, [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i64, i64, i32, i32,

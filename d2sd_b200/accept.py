@@ -45,6 +45,63 @@ class Verifier:
         return acc, self.accepted[:acc], branch
 
 
+class BatchVerifier:
+    """Device buffers of kernel (c) for a batch of R requests of fixed
+    (branches, block_len, vocab): one launch verifies every request
+    (batched serving); results stay on the device."""
+
+    def __init__(self, num_requests: int, num_branches: int, block_len: int, vocab: int, device):
+        self.shape = (num_requests, num_branches, block_len, vocab)
+        self.device = torch.device(device)
+        nbytes = ops.accept_batch_workspace_bytes(num_requests, num_branches, block_len, vocab)
+        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        self.result = torch.zeros(num_requests, 2, dtype=torch.int32, device=self.device)
+        self.accepted = torch.zeros(num_requests, block_len, dtype=torch.int64, device=self.device)
+
+    def launch(self, logits: torch.Tensor, block_ids: torch.Tensor,
+               argmax_out: torch.Tensor | None = None) -> None:
+        if tuple(logits.shape) != self.shape:
+            raise ValueError(f"logits shape {tuple(logits.shape)} != {self.shape}")
+        ops.verify_accept_batch(logits, block_ids, self.result, self.accepted, self.workspace,
+                                argmax_out)
+
+
+class ShardedVerifier:
+    """Vocabulary-sharded kernel (c) on one rank of a KV-head-sharded group:
+    this rank holds columns ``vocab_range`` of the logits; the kernel trades
+    the rows' bests with the other ranks over NVLink (``RecordExchange``) and
+    every rank ends with the same acceptance results."""
+
+    def __init__(self, num_requests: int, num_branches: int, block_len: int, vocab: int, device,
+                 group=None):
+        from .sharding import RecordExchange, vocab_range
+        self.device = torch.device(device)
+        self.exchange = RecordExchange(num_requests * num_branches * block_len, self.device, group)
+        self.vocab = vocab
+        self.columns = vocab_range(vocab, self.exchange.world, self.exchange.rank)
+        width = self.columns[1] - self.columns[0]
+        self.shape = (num_requests, num_branches, block_len, width)
+        nbytes = ops.accept_batch_workspace_bytes(num_requests, num_branches, block_len, width)
+        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        self.result = torch.zeros(num_requests, 2, dtype=torch.int32, device=self.device)
+        self.accepted = torch.zeros(num_requests, block_len, dtype=torch.int64, device=self.device)
+
+    @property
+    def status(self) -> torch.Tensor:
+        return self.exchange.status
+
+    def launch(self, logits_slice: torch.Tensor, block_ids: torch.Tensor,
+               argmax_out: torch.Tensor | None = None) -> None:
+        """logits_slice [R, B, T, V/world]: this rank's columns of the logits."""
+        if tuple(logits_slice.shape) != self.shape:
+            raise ValueError(f"logits slice shape {tuple(logits_slice.shape)} != {self.shape}")
+        ops.verify_accept_sharded(logits_slice, self.columns[0], block_ids, self.result,
+                                  self.accepted, self.workspace, self.exchange, argmax_out)
+
+    def close(self) -> None:
+        self.exchange.close()
+
+
 _verifiers: dict = {}
 
 

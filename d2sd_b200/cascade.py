@@ -105,7 +105,7 @@ def cascade_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                       sinks: torch.Tensor | None = None, sink_mode: str = "reference",
                       shared_tokens: int = 0, custom_mask: torch.Tensor | None = None,
                       plan: CascadePlan | None = None, out: torch.Tensor | None = None,
-                      lse: torch.Tensor | None = None):
+                      lse: torch.Tensor | None = None, status: torch.Tensor | None = None):
     """One layer of the cascade verify attention for one request.
 
     q [B, T, Hq, D] bf16 (the block tokens' queries), k_new/v_new [B, T, Hk, D]
@@ -114,7 +114,9 @@ def cascade_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
     the last window prefix keys (generation/verification.py:130-135);
     ``shared_tokens`` > 0 declares that all branches share their first tokens,
     so their prefix attention is computed once. Returns (out [B, T, Hq, D],
-    lse [B, T, Hq] base 2), written into ``out``/``lse`` when given.
+    lse [B, T, Hq] base 2), written into ``out``/``lse`` when given. Kernel (a)
+    reports a wait time-out in ``plan.status``, kernel (b) in ``status`` (an
+    int32 device tensor, optional).
     """
     B, T, Hq, D = q.shape
     Hk = k_new.shape[2]
@@ -142,5 +144,6 @@ def cascade_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                      mask_mode=mode, custom_mask=custom_mask,
                      partial=plan.partial if plan.num_ctas else None, plan_dev=plan.plan,
                      prefix_token=ptok, sinks=sinks,
-                     sink_mode=_SINKS[sink_mode] if sinks is not None else _lib.SINK_NONE)
+                     sink_mode=_SINKS[sink_mode] if sinks is not None else _lib.SINK_NONE,
+                     status=status)
     return out, lse

@@ -15,11 +15,16 @@
 // Ties resolve to the first maximal index and NaN counts as maximal (first NaN
 // wins), the torch.argmax convention.
 //
-// Work is split into warp items of 2048-element chunks of one logits row (each
-// lane keeps 8 16-byte loads in flight); persistent CTAs walk the items. The
-// warp that finishes a row's last item (per-row atomic count) reduces the row's
-// partials, and the warp that finishes the last row runs the walk, so no
-// single CTA serialises the reduction.
+// Work: the 16-byte vectors of all logits rows, flattened, are split evenly
+// over the grid (stream-K: a CTA's range may cross rows); each thread keeps 8
+// loads in flight and each CTA records one (max, first index) per row segment.
+// The CTA that finishes last (atomic ticket) reduces the segments of every row
+// and runs the walks, one warp per request.
+// Modes: one request (d2sd_verify_accept); a batch of requests with their own
+// logits, ids and results in one launch (d2sd_verify_accept_batch, batched
+// serving); and a vocabulary-sharded launch (d2sd_verify_accept_sharded) in
+// which each rank scans its slice of the vocabulary and the last CTA trades the
+// rows' bests with the other ranks over NVLink before every rank walks.
 #include <mutex>
 #include <string>
 
@@ -217,26 +222,58 @@ __device__ __forceinline__ void scan_units(const T* __restrict__ row, int64_t u0
   }
 }
 
+// Logits rows of one launch: num_requests x num_branches x block_len rows,
+// row r = (request, branch, position) in that order.
+struct Shape {
+  int R, B, TB;
+  int64_t V;
+  int64_t s_r, s_b, s_t;     // logits element strides
+  int64_t i_r, i_b, i_t;     // block id strides
+  int64_t vocab_offset;      // index of logits column 0 in the full vocabulary
+};
+
+// Vocabulary-sharded acceptance: each rank scans its slice of the vocabulary
+// and the per-row bests are exchanged over NVLink before the walk.
+struct AcceptExchange {
+  void* const* rec;                  // [2][world] record buffers ([world][rows] uint4 each)
+  unsigned long long* const* ctl;    // [world] control blocks (uint64[8])
+  int world, rank;
+  int64_t epoch;
+  int32_t* status;
+};
+
+constexpr int A_ARRIVE0 = 0;  // + epoch parity (control block words)
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kThreads)
-    accept_kernel(const T* __restrict__ logits, int B, int TB, int64_t V, int64_t s_b,
-                  int64_t s_t, const int64_t* __restrict__ ids, int64_t ids_sb, int64_t ids_st,
-                  int32_t* result, int64_t* accepted, int64_t* argmax_out, Workspace ws, Part pt) {
+    accept_kernel(const T* __restrict__ logits, Shape sh, const int64_t* __restrict__ ids,
+                  int32_t* result, int64_t* accepted, int64_t* argmax_out, Workspace ws, Part pt,
+                  AcceptExchange ax) {
   __shared__ float sv[kThreads / 32];
   __shared__ int64_t si[kThreads / 32];
   __shared__ bool last;
   __shared__ int32_t s_amax[64 * 64];
   __shared__ int64_t s_ids[kIdsCache];
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int rows = B * TB;
+  const int TB = sh.TB, B = sh.B;
+  const int bt = B * TB;
+  const int rows = sh.R * bt;
   const int64_t u_begin = static_cast<int64_t>(blockIdx.x) * pt.W;
   const int64_t u_end = u_begin + pt.W < pt.total ? u_begin + pt.W : pt.total;
   int seg = 0;
   for (int64_t u = u_begin; u < u_end; ++seg) {
     const int64_t r = u / pt.upr;
     const int64_t re = (r + 1) * pt.upr < u_end ? (r + 1) * pt.upr : u_end;
-    const int b = static_cast<int>(r / TB), t = static_cast<int>(r % TB);
-    const T* base = logits + static_cast<int64_t>(b) * s_b + static_cast<int64_t>(t) * s_t;
+    const int q = static_cast<int>(r / bt);
+    const int b = static_cast<int>((r / TB) % B), t = static_cast<int>(r % TB);
+    const T* base = logits + static_cast<int64_t>(q) * sh.s_r + static_cast<int64_t>(b) * sh.s_b +
+                    static_cast<int64_t>(t) * sh.s_t;
     float bv = -INFINITY;
     int64_t bi = INT64_MAX;
     scan_units<T, VEC>(base, u - r * pt.upr + threadIdx.x, re - r * pt.upr, kThreads, bv, bi);
@@ -270,9 +307,12 @@ __global__ void __launch_bounds__(kThreads)
   // ---- last CTA: stage the block ids, then per-row argmax over the (at most
   // a few) CTA segments of the row ----
   const bool ids_cached = rows <= kIdsCache;
+  auto id_at = [&](int q, int b, int t) -> int64_t {
+    return ids[q * sh.i_r + b * sh.i_b + t * sh.i_t];
+  };
   if (ids_cached) {
     for (int r = threadIdx.x; r < rows; r += kThreads)
-      s_ids[r] = ids[(r / TB) * ids_sb + (r % TB) * ids_st];
+      s_ids[r] = id_at(r / bt, (r / TB) % B, r % TB);
   }
   for (int r = threadIdx.x; r < rows; r += kThreads) {
     const int64_t c_first = (static_cast<int64_t>(r) * pt.upr) / pt.W;
@@ -307,40 +347,96 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
     if (bi == INT64_MAX) bi = 0;
-    s_amax[r] = static_cast<int32_t>(bi);
-    if (argmax_out) argmax_out[r] = bi;
+    bi += sh.vocab_offset;
+    if (ax.world > 0) {
+      // the row's best of this vocabulary slice into every rank's buffer
+      uint4 rec;
+      rec.x = __float_as_uint(bv);
+      rec.y = 0u;
+      rec.z = static_cast<uint32_t>(static_cast<uint64_t>(bi));
+      rec.w = static_cast<uint32_t>(static_cast<uint64_t>(bi) >> 32);
+      void* const* outs = ax.rec + (ax.epoch & 1) * ax.world;
+      for (int d = 0; d < ax.world; ++d)
+        reinterpret_cast<uint4*>(outs[d])[static_cast<int64_t>(ax.rank) * rows + r] = rec;
+    } else {
+      s_amax[r] = static_cast<int32_t>(bi);
+      if (argmax_out) argmax_out[r] = bi;
+    }
+  }
+  if (ax.world > 0) {
+    // signal every rank once, wait (bounded) until every rank's records are
+    // here, then combine the slices' bests in rank (= vocabulary) order: the
+    // first maximal index of the whole row, as the unsharded scan finds it
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      const int par = static_cast<int>(ax.epoch & 1);
+      for (int d = 0; d < ax.world; ++d) atomicAdd_system(ax.ctl[d] + A_ARRIVE0 + par, 1ull);
+      unsigned long long* mine = ax.ctl[ax.rank] + A_ARRIVE0 + par;
+      const uint64_t t0 = global_timer_ns();
+      int ok = 1;
+      while (ld_acquire_sys_u64(mine) < static_cast<unsigned long long>(ax.world)) {
+        if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+          ok = 0;
+          break;
+        }
+      }
+      if (ok) atomicExch(mine, 0ull);
+      else atomicExch(ax.status, 3);
+      s_ok = ok;
+    }
+    __syncthreads();
+    __threadfence_system();
+    const uint4* in = reinterpret_cast<const uint4*>(ax.rec[(ax.epoch & 1) * ax.world + ax.rank]);
+    for (int r = threadIdx.x; r < rows; r += kThreads) {
+      float bv = -INFINITY;
+      int64_t bi = INT64_MAX;
+      for (int k = 0; k < ax.world; ++k) {
+        const uint4 rec = __ldcv(in + static_cast<int64_t>(k) * rows + r);
+        const float vv = __uint_as_float(rec.x);
+        const int64_t ii = static_cast<int64_t>((static_cast<uint64_t>(rec.w) << 32) | rec.z);
+        if (better(vv, ii, bv, bi)) {
+          bv = vv;
+          bi = ii;
+        }
+      }
+      if (!s_ok || bi == INT64_MAX) bi = 0;
+      s_amax[r] = static_cast<int32_t>(bi);
+      if (argmax_out) argmax_out[r] = bi;
+    }
   }
   __syncthreads();
 
-  // ---- the acceptance walk on warp 0 (valid set as a 64-bit mask) ----
-  if (warp == 0) {
+  // ---- the acceptance walks, one warp per request (valid set as a 64-bit mask) ----
+  for (int q = warp; q < sh.R; q += kThreads / 32) {
+    const int r0 = q * bt;
     uint64_t valid = (B >= 64) ? ~0ull : ((1ull << B) - 1ull);
     int acc = 0;
     int vb = 0;
+    int64_t* acc_q = accepted + static_cast<int64_t>(q) * TB;
     while (true) {
       vb = __ffsll(static_cast<long long>(valid)) - 1;
-      const int64_t tok = s_amax[vb * TB + acc];
-      if (lane == 0) accepted[acc] = tok;
+      const int64_t tok = s_amax[r0 + vb * TB + acc];
+      if (lane == 0) acc_q[acc] = tok;
       acc += 1;
       if (acc == TB) break;
       bool m0 = false, m1 = false;
-      if (lane < B)
-        m0 = (ids_cached ? s_ids[lane * TB + acc] : ids[lane * ids_sb + acc * ids_st]) == tok;
+      if (lane < B) m0 = (ids_cached ? s_ids[r0 + lane * TB + acc] : id_at(q, lane, acc)) == tok;
       if (lane + 32 < B)
-        m1 = (ids_cached ? s_ids[(lane + 32) * TB + acc]
-                         : ids[(lane + 32) * ids_sb + acc * ids_st]) == tok;
+        m1 = (ids_cached ? s_ids[r0 + (lane + 32) * TB + acc] : id_at(q, lane + 32, acc)) == tok;
       const uint64_t match = static_cast<uint64_t>(__ballot_sync(0xffffffffu, m0)) |
                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, m1)) << 32);
       valid &= match;
       if (valid == 0) break;
     }
-    for (int k = acc + lane; k < TB; k += 32) accepted[k] = -1;
+    for (int k = acc + lane; k < TB; k += 32) acc_q[k] = -1;
     if (lane == 0) {
-      result[0] = acc;
-      result[1] = vb;
-      *ws.ticket = 0u;  // leave the workspace zeroed for the next launch
+      result[2 * q] = acc;
+      result[2 * q + 1] = vb;
     }
   }
+  if (threadIdx.x == 0) *ws.ticket = 0u;  // leave the workspace zeroed for the next launch
 }
 
 }  // namespace
@@ -351,30 +447,54 @@ namespace {
 int accept_grid() { return current_sm_count() * 3; }
 
 template <typename T>
-int launch_accept(const void* logits, int B, int TB, int64_t V, int64_t sb, int64_t st,
-                  const int64_t* ids, int64_t isb, int64_t ist, int32_t* result, int64_t* acc_ids,
-                  int64_t* argmax_out, void* workspace, int64_t wbytes, cudaStream_t stream) {
+int launch_accept(const void* logits, const Shape& sh, const int64_t* ids, int32_t* result,
+                  int64_t* acc_ids, int64_t* argmax_out, void* workspace, int64_t wbytes,
+                  const AcceptExchange& ax, cudaStream_t stream, const char* what) {
   constexpr int VN = Vec<T>::N;
-  const int64_t rows = static_cast<int64_t>(B) * TB;
+  const int64_t rows = static_cast<int64_t>(sh.R) * sh.B * sh.TB;
   const int grid = accept_grid();
   if (rows > 64 * 64)
-    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: at most 4096 logits rows");
+    return fail(D2SD_ERR_UNSUPPORTED, std::string(what) + ": at most 4096 logits rows");
   if (wbytes < workspace_bytes(rows, grid))
-    return fail(D2SD_ERR_WORKSPACE, "d2sd_verify_accept: workspace too small");
+    return fail(D2SD_ERR_WORKSPACE, std::string(what) + ": workspace too small");
   Workspace ws = carve(workspace, rows, grid);
-  const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && V % VN == 0 &&
-                   sb % VN == 0 && st % VN == 0;
-  const int64_t upr = vec ? V / VN : V;
+  const bool vec = (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && sh.V % VN == 0 &&
+                   sh.s_r % VN == 0 && sh.s_b % VN == 0 && sh.s_t % VN == 0;
+  const int64_t upr = vec ? sh.V / VN : sh.V;
   Part pt = partition(rows, upr, grid);
   if (vec)
-    accept_kernel<T, true><<<grid, kThreads, 0, stream>>>(
-        static_cast<const T*>(logits), B, TB, V, sb, st, ids, isb, ist, result, acc_ids,
-        argmax_out, ws, pt);
+    accept_kernel<T, true><<<grid, kThreads, 0, stream>>>(static_cast<const T*>(logits), sh, ids,
+                                                          result, acc_ids, argmax_out, ws, pt, ax);
   else
-    accept_kernel<T, false><<<grid, kThreads, 0, stream>>>(
-        static_cast<const T*>(logits), B, TB, V, sb, st, ids, isb, ist, result, acc_ids,
-        argmax_out, ws, pt);
+    accept_kernel<T, false><<<grid, kThreads, 0, stream>>>(static_cast<const T*>(logits), sh, ids,
+                                                           result, acc_ids, argmax_out, ws, pt, ax);
   return check_launch("accept_kernel");
+}
+
+int accept_dispatch(const void* logits, int32_t dtype, const Shape& sh, const int64_t* ids,
+                    int32_t* result, int64_t* acc_ids, int64_t* argmax_out, void* workspace,
+                    int64_t wbytes, const AcceptExchange& ax, void* stream, const char* what) {
+  if (!logits || !ids || !result || !acc_ids || !workspace || sh.R <= 0 || sh.B <= 0 ||
+      sh.TB <= 0 || sh.V <= 0 || sh.vocab_offset < 0)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, std::string(what) + ": invalid argument");
+  if (sh.B > kMaxBranches)
+    return fail(D2SD_ERR_UNSUPPORTED, std::string(what) + ": at most 64 branches");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, std::string(what) + ": workspace must be 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case D2SD_DTYPE_F32:
+      return launch_accept<float>(logits, sh, ids, result, acc_ids, argmax_out, workspace, wbytes,
+                                  ax, st, what);
+    case D2SD_DTYPE_BF16:
+      return launch_accept<__nv_bfloat16>(logits, sh, ids, result, acc_ids, argmax_out, workspace,
+                                          wbytes, ax, st, what);
+    case D2SD_DTYPE_F16:
+      return launch_accept<__half>(logits, sh, ids, result, acc_ids, argmax_out, workspace,
+                                   wbytes, ax, st, what);
+    default:
+      return fail(D2SD_ERR_UNSUPPORTED, std::string(what) + ": unknown dtype");
+  }
 }
 }  // namespace
 }  // namespace d2sd
@@ -392,32 +512,61 @@ extern "C" int d2sd_verify_accept(const void* logits, int32_t dtype, int32_t num
                                   int32_t* result, int64_t* accepted_ids, int64_t* argmax_out,
                                   void* workspace, int64_t workspace_bytes, void* stream) {
   using namespace d2sd;
-  if (!logits || !block_ids || !result || !accepted_ids || !workspace || num_branches <= 0 ||
-      block_len <= 0 || vocab <= 0)
-    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_verify_accept: invalid argument");
-  if (num_branches > kMaxBranches)
-    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: at most 64 branches");
-  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
-    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_verify_accept: workspace must be 256-byte aligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (dtype) {
-    case D2SD_DTYPE_F32:
-      return launch_accept<float>(logits, num_branches, block_len, vocab, stride_branch,
-                                  stride_pos, block_ids, ids_stride_branch, ids_stride_pos,
-                                  result, accepted_ids, argmax_out, workspace, workspace_bytes, st);
-    case D2SD_DTYPE_BF16:
-      return launch_accept<__nv_bfloat16>(logits, num_branches, block_len, vocab, stride_branch,
-                                          stride_pos, block_ids, ids_stride_branch,
-                                          ids_stride_pos, result, accepted_ids, argmax_out,
-                                          workspace, workspace_bytes, st);
-    case D2SD_DTYPE_F16:
-      return launch_accept<__half>(logits, num_branches, block_len, vocab, stride_branch,
-                                   stride_pos, block_ids, ids_stride_branch, ids_stride_pos,
-                                   result, accepted_ids, argmax_out, workspace, workspace_bytes,
-                                   st);
-    default:
-      return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept: unknown dtype");
-  }
+  const Shape sh{1, num_branches, block_len, vocab, 0, stride_branch, stride_pos,
+                 0, ids_stride_branch, ids_stride_pos, 0};
+  return accept_dispatch(logits, dtype, sh, block_ids, result, accepted_ids, argmax_out,
+                         workspace, workspace_bytes, AcceptExchange{}, stream,
+                         "d2sd_verify_accept");
+}
+
+extern "C" int64_t d2sd_verify_accept_batch_workspace_size(int32_t num_requests,
+                                                           int32_t num_branches,
+                                                           int32_t block_len, int64_t vocab) {
+  if (num_requests <= 0 || num_branches <= 0 || block_len <= 0 || vocab <= 0) return -1;
+  return d2sd::workspace_bytes(static_cast<int64_t>(num_requests) * num_branches * block_len,
+                               d2sd::accept_grid());
+}
+
+extern "C" int d2sd_verify_accept_batch(const void* logits, int32_t dtype, int32_t num_requests,
+                                        int32_t num_branches, int32_t block_len, int64_t vocab,
+                                        int64_t stride_request, int64_t stride_branch,
+                                        int64_t stride_pos, const int64_t* block_ids,
+                                        int64_t ids_stride_request, int64_t ids_stride_branch,
+                                        int64_t ids_stride_pos, int32_t* result,
+                                        int64_t* accepted_ids, int64_t* argmax_out,
+                                        void* workspace, int64_t workspace_bytes, void* stream) {
+  using namespace d2sd;
+  const Shape sh{num_requests, num_branches, block_len, vocab, stride_request, stride_branch,
+                 stride_pos, ids_stride_request, ids_stride_branch, ids_stride_pos, 0};
+  return accept_dispatch(logits, dtype, sh, block_ids, result, accepted_ids, argmax_out,
+                         workspace, workspace_bytes, AcceptExchange{}, stream,
+                         "d2sd_verify_accept_batch");
+}
+
+extern "C" int d2sd_verify_accept_sharded(
+    const void* logits, int32_t dtype, int32_t num_requests, int32_t num_branches,
+    int32_t block_len, int64_t vocab_slice, int64_t vocab_offset, int64_t stride_request,
+    int64_t stride_branch, int64_t stride_pos, const int64_t* block_ids,
+    int64_t ids_stride_request, int64_t ids_stride_branch, int64_t ids_stride_pos,
+    int32_t* result, int64_t* accepted_ids, int64_t* argmax_out, void* workspace,
+    int64_t workspace_bytes, void* const* record_ptrs, uint64_t* const* control_ptrs,
+    int32_t world, int32_t rank, int64_t epoch, int32_t* status, void* stream) {
+  using namespace d2sd;
+  if (!record_ptrs || !control_ptrs || !status || world <= 0 || rank < 0 || rank >= world ||
+      epoch <= 0)
+    return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_verify_accept_sharded: invalid exchange argument");
+  const Shape sh{num_requests, num_branches, block_len, vocab_slice, stride_request,
+                 stride_branch, stride_pos, ids_stride_request, ids_stride_branch,
+                 ids_stride_pos, vocab_offset};
+  AcceptExchange ax;
+  ax.rec = record_ptrs;
+  ax.ctl = reinterpret_cast<unsigned long long* const*>(control_ptrs);
+  ax.world = world;
+  ax.rank = rank;
+  ax.epoch = epoch;
+  ax.status = status;
+  return accept_dispatch(logits, dtype, sh, block_ids, result, accepted_ids, argmax_out,
+                         workspace, workspace_bytes, ax, stream, "d2sd_verify_accept_sharded");
 }
 
 // ---------------------------------------------------------------------------
@@ -434,8 +583,9 @@ extern "C" int d2sd_verify_accept(const void* logits, int32_t dtype, int32_t num
 //
 // In host code `g_accept_scratch` is only a host-side stand-in for the device
 // array; its device address is fetched with cudaGetSymbolAddress, once per
-// device, on the first call made with that device current. That first call
-// should therefore happen before any stream capture. All calls share the one
+// device, on the first call made with that device current (and again if the
+// device's context has changed since, as after cudaDeviceReset). That first
+// call should therefore happen before any stream capture. All calls share the one
 // array and it keeps the previous call's contents: the ticket is cleared on
 // the caller's stream before every launch, and calls whose kernels overlap on
 // the GPU (e.g. issued on two streams at once) race on the array.
@@ -446,9 +596,37 @@ namespace {
 constexpr int64_t kStaticScratchBytes = 256 * 1024;
 static __device__ __align__(256) uint8_t g_accept_scratch[kStaticScratchBytes];
 
+// Unique id of the current CUDA context (cuCtxGetId through the runtime's
+// driver entry point), 0 if it cannot be read. A device reset or a recreated
+// primary context gets a new id, and with it a new copy of the array.
+unsigned long long current_context_id() {
+  using GetCur = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCur get_cur = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<GetCur>(p);
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_cur || !get_id || get_cur(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
 int static_scratch(void** out) {
   static std::mutex mu;
   static void* addr[64] = {};
+  static unsigned long long ctx_of[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess)
@@ -456,13 +634,17 @@ int static_scratch(void** out) {
   if (dev < 0 || dev >= 64)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_verify_accept_noalloc: device index above 63");
   std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+  const unsigned long long ctx = current_context_id();
+  // the address is looked up again whenever the context changed (or its id is
+  // unknown), so it never outlives a device reset
+  if (addr[dev] == nullptr || ctx == 0 || ctx != ctx_of[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_accept_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(D2SD_ERR_CUDA, std::string("cudaGetSymbolAddress(g_accept_scratch): ") +
                                      cudaGetErrorString(e));
     addr[dev] = p;
+    ctx_of[dev] = current_context_id();  // the lookup has created the context if needed
   }
   *out = addr[dev];
   return D2SD_OK;

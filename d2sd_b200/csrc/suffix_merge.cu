@@ -54,12 +54,21 @@ struct SuffixParams {
   int32_t rows_per_cta;  // merge rows of a CTA: 64, 32 or 16 (128-row tile / parts)
   float scale_log2;
   // fused output exchange (d2sd_suffix_merge_gather); world == 0: rows go to out
-  void* const* peer_out;
-  unsigned long long* const* peer_ctr;
+  void* const* peer_out;               // [2][world]: output buffers of each epoch parity
+  unsigned long long* const* peer_ctr;  // [world]: each rank's exchange control block
   int32_t world, rank, head_offset;
   int64_t pg_st, pg_sh;
   int64_t epoch;
 };
+
+// Exchange control block of one rank (uint64 words, zero before the first call):
+// arrivals of the ranks' calls of even / odd epochs, the CTA ticket of the
+// running call, and wait statistics of this rank's calls.
+constexpr int X_ARRIVE0 = 0;   // + epoch parity
+constexpr int X_TICKET = 2;
+constexpr int X_WAIT_NS = 3;   // total time the signalling CTA waited for the peers
+constexpr int X_WAITS = 4;     // number of completed waits
+constexpr int X_WAIT_MAX = 5;  // longest wait
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
   unsigned long long v;
@@ -482,12 +491,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < VEC; ++c) reinterpret_cast<uint4*>(orow)[c] = o[c];
     } else {
-      // the row into every rank's output, at this rank's head offset (NVLink
-      // stores for the peers)
+      // the row into every rank's output buffer of this epoch's parity, at this
+      // rank's head offset (NVLink stores for the peers)
       const int64_t off = static_cast<int64_t>(mt.tok) * p.pg_st +
                           static_cast<int64_t>(p.head_offset + mt.hq) * p.pg_sh + j8 * CPL;
+      void* const* outs = p.peer_out + (p.epoch & 1) * p.world;
       for (int d = 0; d < p.world; ++d) {
-        T* orow = static_cast<T*>(p.peer_out[d]) + off;
+        T* orow = static_cast<T*>(outs[d]) + off;
 #pragma unroll
         for (int c = 0; c < VEC; ++c) reinterpret_cast<uint4*>(orow)[c] = o[c];
       }
@@ -495,25 +505,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (j8 == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
   }
   if (p.world > 0) {
-    // arrival: this CTA's rows are in every rank's buffer. CTA 0 then waits
-    // (bounded) for every CTA of every rank, so that this kernel completes only
-    // when this rank's buffer is whole
+    // Arrival. Every CTA makes its peer stores visible system-wide and takes a
+    // ticket; the CTA that takes the last one signals every rank once (one
+    // NVLink atomic per peer per call instead of one per CTA) and then waits,
+    // bounded, until every rank has signalled this rank, so that the kernel
+    // completes only when this rank's buffer is whole.
+    // The arrival counters alternate with the epoch parity and the waiting CTA
+    // resets its own before the kernel completes: a peer can add to the same
+    // counter again (epoch + 2) only after this rank has signalled epoch + 1,
+    // which its stream does only after this kernel has completed. Hence the
+    // count to wait for is world, whatever the grid of this call or the last.
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence_system();
-      for (int d = 0; d < p.world; ++d) atomicAdd_system(p.peer_ctr[d], 1ull);
-      if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) {
-        const unsigned long long expected = static_cast<unsigned long long>(p.epoch) *
-                                            static_cast<unsigned long long>(p.world) * gridDim.x *
-                                            gridDim.y * gridDim.z;
-        const unsigned long long* mine = p.peer_ctr[p.rank];
+      unsigned long long* mine = p.peer_ctr[p.rank];
+      const unsigned long long ctas =
+          static_cast<unsigned long long>(gridDim.x) * gridDim.y * gridDim.z;
+      if (atomicAdd(mine + X_TICKET, 1ull) == ctas - 1) {
+        __threadfence_system();
+        const int par = static_cast<int>(p.epoch & 1);
+        for (int d = 0; d < p.world; ++d) atomicAdd_system(p.peer_ctr[d] + X_ARRIVE0 + par, 1ull);
         const uint64_t t0 = global_timer_ns();
-        while (ld_acquire_sys(mine) < expected) {
+        bool ok = true;
+        while (ld_acquire_sys(mine + X_ARRIVE0 + par) < static_cast<unsigned long long>(p.world)) {
           if (global_timer_ns() - t0 > kWaitTimeoutNs) {
-            if (p.status) atomicExch(p.status, 3);
+            ok = false;
             break;
           }
         }
+        const unsigned long long waited = global_timer_ns() - t0;
+        if (ok) {
+          atomicExch(mine + X_ARRIVE0 + par, 0ull);
+          atomicAdd(mine + X_WAIT_NS, waited);
+          atomicAdd(mine + X_WAITS, 1ull);
+          atomicMax(mine + X_WAIT_MAX, waited);
+        } else {
+          // a peer never arrived: the counter is left as it is (late arrivals may
+          // still land) and the caller must treat the exchange as failed
+          atomicExch(p.status, 3);
+        }
+        atomicExch(mine + X_TICKET, 0ull);
         __threadfence_system();
       }
     }
@@ -782,6 +813,10 @@ extern "C" int d2sd_suffix_merge_gather(
   if (!out_ptrs || !counters || world <= 0 || rank < 0 || rank >= world || head_offset < 0 ||
       epoch <= 0)
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge_gather: invalid exchange argument");
+  if (!status)
+    return fail(D2SD_ERR_INVALID_ARGUMENT,
+                "d2sd_suffix_merge_gather: a status word is required (it reports a peer that "
+                "never arrived)");
   if (peer_stride_token % 8 || peer_stride_head % 8)
     return fail(D2SD_ERR_INVALID_ARGUMENT,
                 "d2sd_suffix_merge_gather: output strides must be multiples of 8 elements");

@@ -172,3 +172,93 @@ class PagedKVCache:
                       umma_pages=self.layout == "umma", **hkw)
         if advance_by is not None:
             self.length = start + int(advance_by)
+
+
+class PagedKVPool(PagedKVCache):
+    """Paged target caches of many sequences in one pool per layer (batched
+    serving: each request of the batch is one sequence).
+
+    Sequence s owns the pages page_table[page_offsets[s] : page_offsets[s] +
+    pages_of(s)], so its position p lives in page page_table[page_offsets[s] +
+    p // 16] -- the per-request page-table offset kernel (a) and the batched
+    commit take. ``lengths_dev`` (int32, device) holds every sequence's cache
+    length for the batched commit, which appends each request's accepted rows
+    in one launch (``commit_batch``).
+    """
+
+    def __init__(self, num_layers: int, num_kv_heads: int, head_dim: int, capacities,
+                 page_size: int = 16, dtype: torch.dtype = torch.bfloat16, device="cuda",
+                 shuffle_seed: int | None = None, layout: str = "umma"):
+        caps = [int(c) for c in capacities]
+        pages = [-(-c // page_size) for c in caps]
+        offsets, cur = [], 0
+        for n in pages:
+            offsets.append(cur)
+            cur += n
+        order = (torch.randperm(max(cur, 1), generator=torch.Generator().manual_seed(shuffle_seed))
+                 if shuffle_seed is not None else torch.arange(max(cur, 1)))
+        super().__init__(num_layers, num_kv_heads, head_dim, max(cur, 1) * page_size, page_size,
+                         dtype, device, page_order=order, layout=layout)
+        self.capacities = caps
+        self.page_offsets_host = offsets
+        self.page_offsets = torch.tensor(offsets, dtype=torch.int32, device=self.device)
+        self.lengths = [0] * len(caps)
+        self.lengths_dev = torch.zeros(len(caps), dtype=torch.int32, device=self.device)
+
+    @property
+    def num_seqs(self) -> int:
+        return len(self.capacities)
+
+    def set_lengths(self, lengths) -> None:
+        self.lengths = [int(x) for x in lengths]
+        self.lengths_dev.copy_(torch.tensor(self.lengths, dtype=torch.int32))
+
+    def write_seq(self, l: int, s: int, k: torch.Tensor, v: torch.Tensor, start: int = 0) -> None:
+        """Write k, v [n, Hk, D] at positions start.. of sequence s, layer l."""
+        if start + k.shape[0] > self.capacities[s]:
+            raise ValueError("sequence capacity exceeded")
+        self.write(l, k, v, start=self.page_offsets_host[s] * self.page_size + start)
+
+    def gather_seq(self, l: int, s: int, length: int):
+        """Sequence s of layer l as contiguous [length, Hk, D] tensors (for checks)."""
+        base = self.page_offsets_host[s] * self.page_size
+        pos = torch.arange(base, base + length, device=self.device)
+        page, slot = self.positions_to_slots(pos)
+        if self.layout == "hnd":
+            return self.k[l, page, :, slot], self.v[l, page, :, slot]
+        out = []
+        for pool in (self.k, self.v):
+            blk = self._block_view(pool)[l]
+            out.append(blk[page, :, slot // 8, slot % 8].reshape(length, self.num_kv_heads,
+                                                                   self.head_dim))
+        return out[0], out[1]
+
+    def commit_batch(self, new_k, new_v, accept_results: torch.Tensor, num_branches: int) -> None:
+        """Append every sequence's accepted rows (kernel (d), one launch).
+
+        new_k/new_v: per-layer [S * num_branches, Hk, T, D] tensors (request s,
+        branch b at row s * num_branches + b; a list or a stacked [L, ...]
+        tensor) with identical strides; accept_results: int32 [S, 2] from
+        ``BatchVerifier``. Rows land at each sequence's ``lengths_dev`` onward;
+        the lengths are not advanced (the caller reads acc when it needs it)."""
+        if isinstance(new_k, torch.Tensor):
+            new_k = [new_k[l] for l in range(new_k.shape[0])]
+            new_v = [new_v[l] for l in range(new_v.shape[0])]
+        if len(new_k) != self.num_layers or len(new_v) != self.num_layers:
+            raise ValueError("one new K/V tensor per layer is required")
+        s = new_k[0].stride()
+        for t in list(new_k) + list(new_v):
+            if t.stride() != s or t.dtype != self.dtype or t.stride(-1) != 1:
+                raise ValueError("new K/V tensors must share strides and the cache dtype")
+        RB, Hk, T, D = new_k[0].shape
+        if RB != self.num_seqs * num_branches:
+            raise ValueError("new K/V rows must be sequences x branches")
+        kl = self.k[0]
+        ops.commit_kv_batch(self._layer_ptrs(new_k, new_v), num_layers=self.num_layers,
+                            num_requests=self.num_seqs, num_kv_heads=Hk, head_dim=D,
+                            elem_bytes=self.k.element_size(), block_len=T,
+                            new_strides=(num_branches * s[0], s[0], s[1], s[2]),
+                            cache_strides=(kl.stride(0), kl.stride(2), kl.stride(1)),
+                            page_size=self.page_size, page_table=self.page_table,
+                            page_table_offset=self.page_offsets, accept_results=accept_results,
+                            cache_lens=self.lengths_dev, umma_pages=self.layout == "umma")

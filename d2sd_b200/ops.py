@@ -179,8 +179,11 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
     k/v_local [tokens, Hk, D], lse/prefix_lse [tokens, Hq].
 
     exchange: a ``sharding.PeerExchange``; the merged rows then go into every
-    rank's exchange buffer at this rank's head offset (``out`` is not written)
-    and the launch completes once all ranks' rows are in this rank's buffer."""
+    rank's exchange buffer of this call's epoch parity at this rank's head
+    offset (``out`` is not written; ``exchange.buffer`` is the result) and the
+    launch completes once all ranks' rows are in this rank's buffer. Without a
+    ``status`` tensor the exchange's own (``exchange.status``) receives the
+    time-out code."""
     dev = _require_cuda(q, k_local, v_local, out, lse, custom_mask, partial, plan_dev,
                         prefix_token, prefix_out, prefix_lse, sinks, status)
     for t in (q, k_local, v_local, out, prefix_out):
@@ -209,14 +212,18 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
     if exchange is None:
         check(load().d2sd_suffix_merge(*args, _ptr(status), _stream(dev)), "d2sd_suffix_merge")
         return
-    if exchange.buffer.dtype != out.dtype or exchange.buffer.shape[-1] != D:
+    if exchange.buffers.dtype != out.dtype or exchange.buffers.shape[-1] != D:
         raise ValueError("exchange buffer must match the output dtype and head_dim")
-    epoch = exchange.next_epoch()
-    st = exchange.buffer.stride()
+    if exchange.buffers.device != dev:
+        raise ValueError("exchange buffers must be on the launch device")
+    st = exchange.buffers[0].stride()
+    epoch = exchange.epoch + 1
     check(load().d2sd_suffix_merge_gather(
         *args, exchange.out_ptrs.data_ptr(), exchange.counter_ptrs.data_ptr(), exchange.world,
-        exchange.rank, int(exchange.head_offset), st[0], st[1], epoch, _ptr(status), _stream(dev)),
+        exchange.rank, int(exchange.head_offset), st[0], st[1], epoch,
+        _ptr(status if status is not None else exchange.status), _stream(dev)),
         "d2sd_suffix_merge_gather")
+    exchange.next_epoch()  # only a launched call advances the epoch
 
 
 def merge_state(v: torch.Tensor, s: torch.Tensor, v_other: torch.Tensor,
@@ -267,6 +274,67 @@ def verify_accept(logits: torch.Tensor, block_ids: torch.Tensor, result: torch.T
     check(rc, "d2sd_verify_accept")
 
 
+def accept_batch_workspace_bytes(num_requests: int, num_branches: int, block_len: int,
+                                 vocab: int) -> int:
+    return int(load().d2sd_verify_accept_batch_workspace_size(num_requests, num_branches,
+                                                               block_len, vocab))
+
+
+def _check_batch(logits, block_ids, result, accepted_ids):
+    if logits.dim() != 4 or logits.stride(-1) != 1:
+        raise ValueError("logits must be [requests, branches, block, vocab], vocab contiguous")
+    R, B, T, _ = logits.shape
+    if block_ids.shape != (R, B, T) or block_ids.dtype != torch.int64:
+        raise ValueError("block_ids must be int64 [requests, branches, block]")
+    if result.dtype != torch.int32 or not result.is_contiguous() or result.numel() < 2 * R:
+        raise ValueError("result must be contiguous int32 [requests, 2]")
+    if (accepted_ids.dtype != torch.int64 or not accepted_ids.is_contiguous()
+            or accepted_ids.numel() < R * T):
+        raise ValueError("accepted_ids must be contiguous int64 [requests, block]")
+    return R, B, T
+
+
+def verify_accept_batch(logits: torch.Tensor, block_ids: torch.Tensor, result: torch.Tensor,
+                        accepted_ids: torch.Tensor, workspace: torch.Tensor,
+                        argmax_out: torch.Tensor | None = None) -> None:
+    """Kernel (c) over a batch of requests: logits [R, B, T, V], block_ids int64
+    [R, B, T], result int32 [R, 2], accepted_ids int64 [R, T]."""
+    dev = _require_cuda(logits, block_ids, result, accepted_ids, workspace, argmax_out)
+    R, B, T = _check_batch(logits, block_ids, result, accepted_ids)
+    V = logits.shape[-1]
+    ls, ids = logits.stride(), block_ids.stride()
+    check(load().d2sd_verify_accept_batch(
+        logits.data_ptr(), dtype_code(logits), R, B, T, V, ls[0], ls[1], ls[2],
+        block_ids.data_ptr(), ids[0], ids[1], ids[2], result.data_ptr(), accepted_ids.data_ptr(),
+        _ptr(argmax_out), workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+        _stream(dev)), "d2sd_verify_accept_batch")
+
+
+def verify_accept_sharded(logits_slice: torch.Tensor, vocab_offset: int, block_ids: torch.Tensor,
+                          result: torch.Tensor, accepted_ids: torch.Tensor,
+                          workspace: torch.Tensor, exchange,
+                          argmax_out: torch.Tensor | None = None) -> None:
+    """Vocabulary-sharded kernel (c): logits_slice [R, B, T, V/world] holds
+    columns [vocab_offset, vocab_offset + V/world) of the full vocabulary;
+    ``exchange`` is a ``sharding.RecordExchange``. Results as
+    verify_accept_batch, identical on every rank."""
+    dev = _require_cuda(logits_slice, block_ids, result, accepted_ids, workspace, argmax_out)
+    R, B, T = _check_batch(logits_slice, block_ids, result, accepted_ids)
+    rows = R * B * T
+    if rows > exchange.rows:
+        raise ValueError(f"{rows} logits rows exceed the exchange's {exchange.rows}")
+    ls, ids = logits_slice.stride(), block_ids.stride()
+    epoch = exchange.epoch + 1
+    check(load().d2sd_verify_accept_sharded(
+        logits_slice.data_ptr(), dtype_code(logits_slice), R, B, T, logits_slice.shape[-1],
+        int(vocab_offset), ls[0], ls[1], ls[2], block_ids.data_ptr(), ids[0], ids[1], ids[2],
+        result.data_ptr(), accepted_ids.data_ptr(), _ptr(argmax_out), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), exchange.record_ptrs.data_ptr(),
+        exchange.control_ptrs.data_ptr(), exchange.world, exchange.rank, epoch,
+        exchange.status.data_ptr(), _stream(dev)), "d2sd_verify_accept_sharded")
+    exchange.next_epoch()
+
+
 # ---------------------------------------------------------------------------
 # (d) KV commit
 # ---------------------------------------------------------------------------
@@ -303,6 +371,28 @@ def commit_kv(layer_ptrs: torch.Tensor, *, num_layers: int, num_kv_heads: int, h
         *args, hidden_src_ptrs.data_ptr(), int(hidden_src_ptrs.numel()), int(hidden_size),
         int(hidden_elem_bytes), int(hidden_strides[0]), int(hidden_strides[1]),
         hidden_dst.data_ptr(), hidden_dst.stride(0), _stream(dev)), "d2sd_commit_kv_hidden")
+
+
+def commit_kv_batch(layer_ptrs: torch.Tensor, *, num_layers: int, num_requests: int,
+                    num_kv_heads: int, head_dim: int, elem_bytes: int, block_len: int,
+                    new_strides: tuple[int, int, int, int], cache_strides: tuple[int, int, int],
+                    page_size: int, page_table: torch.Tensor, page_table_offset: torch.Tensor,
+                    accept_results: torch.Tensor, cache_lens: torch.Tensor,
+                    umma_pages: bool = False) -> None:
+    """Kernel (d) for a batch of requests sharing one page pool per layer;
+    new_strides = (request, branch, head, token) element strides of each layer's
+    new K/V; accept_results int32 [R, 2]; cache_lens int32 [R] on the device."""
+    dev = _require_cuda(layer_ptrs, page_table, page_table_offset, accept_results, cache_lens)
+    for t, what in ((page_table_offset, "page_table_offset"), (accept_results, "accept_results"),
+                    (cache_lens, "cache_lens"), (page_table, "page_table")):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{what} must be a contiguous int32 tensor")
+    check(load().d2sd_commit_kv_batch(
+        layer_ptrs.data_ptr(), num_layers, num_requests, num_kv_heads, head_dim, elem_bytes,
+        block_len, *new_strides, *cache_strides, page_size,
+        _lib.KV_UMMA_PAGES if umma_pages else _lib.KV_ROWS, page_table.data_ptr(),
+        page_table_offset.data_ptr(), accept_results.data_ptr(), cache_lens.data_ptr(),
+        _stream(dev)), "d2sd_commit_kv_batch")
 
 
 # ---------------------------------------------------------------------------

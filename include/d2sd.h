@@ -24,8 +24,13 @@
  *       the greedy acceptance walk generation/d3_generator.py:204-225 with
  *       model/utils.py:28-32 (sample, temperature 0), and its single-branch
  *       form generation/dflash_generator.py:110-125.
- *   d2sd_commit_kv
- *       the accepted-branch KV append generation/d3_generator.py:227-232.
+ *   d2sd_verify_accept_batch / d2sd_verify_accept_sharded
+ *       the same walk for a batch of requests in one launch, and its
+ *       vocabulary-sharded multi-GPU form (no reference counterpart: the
+ *       reference verifies one request on one GPU).
+ *   d2sd_commit_kv / d2sd_commit_kv_batch
+ *       the accepted-branch KV append generation/d3_generator.py:227-232 (one
+ *       request, or a batch of requests sharing one page pool).
  *   d2sd_qk_norm_rope
  *       the step before the attention, generation/verification.py:113-124:
  *       attn.q_norm / attn.k_norm (transformers' Qwen3RMSNorm; skipped for
@@ -199,19 +204,29 @@ int d2sd_suffix_merge(const void* q, int64_t q_stride_token,
  * epilogue (KV-head sharding, one process per GPU). It replaces
  * torch.distributed.all_gather_into_tensor of each rank's attention output
  * (the one collective of the KV-head-sharded verify step); the reference runs
- * on one GPU and has no counterpart. Every merged row is stored into the head
- * slice [head_offset, head_offset + num_qo_heads) of each of the `world` output
- * buffers out_ptrs[0..world) (this rank's and its peers', peer ones mapped with
- * d2sd_ipc_open), all with element strides (peer_stride_token,
- * peer_stride_head); `out` is not written. Each CTA then adds 1 to every
- * rank's arrival counter counters[r] (uint64, zero before the first call), and
- * one CTA waits until this rank's counter reaches epoch * world * (number of
- * CTAs), so the kernel completes only once every rank's rows have landed in
- * this rank's buffer. epoch counts the calls on these counters (1, 2, ...),
- * identical on every rank, and every rank must launch the same shapes. The
- * wait is bounded (2 s); on time-out status receives 3. out_ptrs and counters
- * are device arrays of device pointers. Rows are stored with 16-byte vectors:
- * the output bases must be 16-byte aligned and the strides multiples of 8. */
+ * on one GPU and has no counterpart.
+ *
+ * epoch counts this exchange's calls (1, 2, ...), identical on every rank, and
+ * all ranks launch the same shapes in the same call. Outputs are double
+ * buffered by the epoch's parity: out_ptrs is a device array of 2 * world
+ * pointers, [parity][rank] (peer ones mapped with d2sd_ipc_open), and every
+ * merged row is stored into the head slice [head_offset, head_offset +
+ * num_qo_heads) of the `world` buffers out_ptrs[(epoch & 1) * world + r], with
+ * element strides (peer_stride_token, peer_stride_head); `out` is not written.
+ * counters: device array of `world` pointers to each rank's control block of 8
+ * uint64 words, zero before the first call: [0], [1] arrivals of even / odd
+ * epochs, [2] a CTA ticket, [3] total and [5] longest time (ns) this rank's
+ * signalling CTA waited for its peers, [4] the number of such waits.
+ * The last CTA of the call signals every rank once and waits until every rank
+ * has signalled this rank, so the kernel completes only once every rank's rows
+ * have landed in this rank's buffer of this parity.
+ * Consumption contract: the rows of call e may be read by work enqueued on this
+ * rank's stream after call e and before call e + 1 (e.g. o_proj); peers write
+ * call e + 2 into the same buffer only after this rank's call e + 1 has begun
+ * its epilogue. The wait is bounded (2 s); on time-out *status receives 3 and
+ * the exchange must be abandoned. status is required. Rows are stored with
+ * 16-byte vectors: the output bases must be 16-byte aligned and the strides
+ * multiples of 8. */
 int d2sd_suffix_merge_gather(const void* q, int64_t q_stride_token,
                              int64_t q_stride_head, const void* k_local,
                              const void* v_local, int64_t kv_stride_token,
@@ -276,15 +291,77 @@ int d2sd_verify_accept(const void* logits, int32_t dtype,
                        int64_t* accepted_ids, int64_t* argmax_out,
                        void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Workspace bytes for d2sd_verify_accept_batch / _sharded (same rules as
+ * d2sd_verify_accept_workspace_size). */
+int64_t d2sd_verify_accept_batch_workspace_size(int32_t num_requests,
+                                                int32_t num_branches,
+                                                int32_t block_len, int64_t vocab);
+
+/* Greedy acceptance of num_requests independent requests in one launch
+ * (batched serving): the walk of generation/d3_generator.py:204-225 for each
+ * request, as d2sd_verify_accept does for one. Request q's logits are
+ * [num_branches, block_len, vocab] at q*stride_request elements, its block ids
+ * at q*ids_stride_request; result is int32 [num_requests][2] ({acceptance
+ * length, branch} per request), accepted_ids int64 [num_requests][block_len],
+ * argmax_out (or NULL) int64 [num_requests][num_branches][block_len].
+ * num_requests * num_branches * block_len <= 4096. */
+int d2sd_verify_accept_batch(const void* logits, int32_t dtype,
+                             int32_t num_requests, int32_t num_branches,
+                             int32_t block_len, int64_t vocab,
+                             int64_t stride_request, int64_t stride_branch,
+                             int64_t stride_pos, const int64_t* block_ids,
+                             int64_t ids_stride_request,
+                             int64_t ids_stride_branch, int64_t ids_stride_pos,
+                             int32_t* result, int64_t* accepted_ids,
+                             int64_t* argmax_out, void* workspace,
+                             int64_t workspace_bytes, void* stream);
+
+/* Vocabulary-sharded form of d2sd_verify_accept_batch for KV-head-sharded
+ * verification on several GPUs (one process per GPU): rank `rank` of `world`
+ * passes only its slice of every logits row, columns [vocab_offset,
+ * vocab_offset + vocab_slice) of the full vocabulary, with the slices of ranks
+ * 0..world-1 in ascending order. Each rank scans its slice; the CTA that
+ * finishes last stores every row's (max, first index) record into every
+ * rank's record buffer over NVLink, signals each rank once, waits (bounded,
+ * 2 s) for every rank's records and combines them in rank order, which yields
+ * the first maximal index of the whole row (torch.argmax). Every rank then runs
+ * the same walks and writes the same results (indices are full-vocabulary).
+ * The reference runs acceptance on one GPU and has no counterpart; this
+ * replaces a replicated full-vocabulary scan on every rank.
+ * record_ptrs: device array of 2 * world pointers, [epoch parity][rank], each a
+ * buffer of world * rows 16-byte records (rows = num_requests * num_branches *
+ * block_len); control_ptrs: device array of world pointers to each rank's
+ * control block (8 uint64, zero before the first call; [0], [1] are the
+ * arrival counters of even / odd epochs). epoch counts the calls (1, 2, ...),
+ * identical on every rank. status is required and receives 3 if a rank did
+ * not arrive in time. */
+int d2sd_verify_accept_sharded(const void* logits, int32_t dtype,
+                               int32_t num_requests, int32_t num_branches,
+                               int32_t block_len, int64_t vocab_slice,
+                               int64_t vocab_offset, int64_t stride_request,
+                               int64_t stride_branch, int64_t stride_pos,
+                               const int64_t* block_ids,
+                               int64_t ids_stride_request,
+                               int64_t ids_stride_branch, int64_t ids_stride_pos,
+                               int32_t* result, int64_t* accepted_ids,
+                               int64_t* argmax_out, void* workspace,
+                               int64_t workspace_bytes,
+                               void* const* record_ptrs,
+                               uint64_t* const* control_ptrs, int32_t world,
+                               int32_t rank, int64_t epoch, int32_t* status,
+                               void* stream);
+
 /* d2sd_verify_accept without a workspace argument and without allocating.
  * No counterpart in the reference: it exists for callers that cannot provide
  * or allocate device memory at call time -- a runtime whose memory planner owns
  * every allocation, or code running inside a CUDA graph capture. The scratch is
  * a static 256 KiB device array in the library (held by every GPU that loads
  * it until exit); shapes needing more are rejected with D2SD_ERR_UNSUPPORTED.
- * Its device address is looked up on the first call per device, so make that
- * first call before any stream capture. All calls share the array: calls that
- * overlap on the GPU race. Other arguments and results as d2sd_verify_accept. */
+ * Its device address is looked up on the first call per device (and again
+ * when the device's context has changed, e.g. after cudaDeviceReset), so make
+ * that first call before any stream capture. All calls share the array: calls
+ * that overlap on the GPU race. Other arguments and results as
+ * d2sd_verify_accept. */
 int d2sd_verify_accept_noalloc(const void* logits, int32_t dtype,
                                int32_t num_branches, int32_t block_len,
                                int64_t vocab, int64_t stride_branch,
@@ -318,6 +395,27 @@ int d2sd_commit_kv(const void* const* layer_ptrs, int32_t num_layers,
                    const int32_t* accept_result,
                    const int32_t* cache_len_dev, int64_t cache_len_host,
                    void* stream);
+
+/* d2sd_commit_kv for num_requests independent requests in one launch
+ * (batched serving; the reference's per-request append of
+ * generation/d3_generator.py:227-232). All requests' caches share one pool per
+ * layer (layer_ptrs as in d2sd_commit_kv); request q's page table starts at
+ * page_table[page_table_offset[q]], its new K/V at q*new_stride_request
+ * elements of each layer's new_k/new_v, its acceptance result at
+ * accept_results[2q] (as written by d2sd_verify_accept_batch) and its cache
+ * length at cache_lens[q] (device int32). */
+int d2sd_commit_kv_batch(const void* const* layer_ptrs, int32_t num_layers,
+                         int32_t num_requests, int32_t num_kv_heads,
+                         int32_t head_dim, int32_t elem_bytes,
+                         int32_t block_len, int64_t new_stride_request,
+                         int64_t new_stride_branch, int64_t new_stride_head,
+                         int64_t new_stride_token, int64_t cache_stride_page,
+                         int64_t cache_stride_slot, int64_t cache_stride_head,
+                         int32_t page_size, int32_t cache_format,
+                         const int32_t* page_table,
+                         const int32_t* page_table_offset,
+                         const int32_t* accept_results,
+                         const int32_t* cache_lens, void* stream);
 
 /* Per-head RMSNorm (optional) and rotary embedding of the block's q and k in
  * one launch, with the 16-bit roundings of the reference's eager expressions:

@@ -32,30 +32,48 @@ def single_prefill(q, k, v, causal: bool = False, sm_scale: float | None = None,
     j <= i + (P - N). Keys before kv_start are invisible (a sliding window).
     Returns (out [N, Hq, D] float64, lse [N, Hq] float64 base 2); a row with no
     visible key gets out = 0 and lse = -inf.
+    Computed one kv head (its G query heads) and one block of query rows at a
+    time with float64 matrix products on the CPU (torch, multi-threaded), so
+    that long prefixes (32768 keys) fit and finish in seconds.
     """
     q, k, v = _to64(q), _to64(k), _to64(v)
     N, Hq, D = q.shape
     P, Hk, _ = k.shape
     G = Hq // Hk
     scale = D ** -0.5 if sm_scale is None else float(sm_scale)
-    kh = np.repeat(k, G, axis=1)  # [P, Hq, D]
-    vh = np.repeat(v, G, axis=1)
-    s = np.einsum("nhd,phd->hnp", q, kh) * scale  # [Hq, N, P]
-    visible = np.ones((N, P), dtype=bool)
-    if causal:
-        visible &= np.arange(P)[None, :] <= (np.arange(N)[:, None] + (P - N))
-    if kv_start > 0:
-        visible &= np.arange(P)[None, :] >= kv_start
-    s = np.where(visible[None], s, -np.inf)
-    m = s.max(axis=-1, keepdims=True)
-    has = np.isfinite(m)
-    m_safe = np.where(has, m, 0.0)
-    p = np.exp(s - m_safe)
-    l = p.sum(axis=-1, keepdims=True)
-    out = np.einsum("hnp,phd->nhd", p, vh) / np.where(l > 0, l, 1.0).transpose(1, 0, 2)
-    lse = np.where(has[..., 0], (m_safe[..., 0] + np.log(np.where(l[..., 0] > 0, l[..., 0], 1.0)))
-                   * LOG2E, -np.inf)  # [Hq, N]
-    return out, lse.T.copy()
+    out = np.zeros((N, Hq, D))
+    lse = np.full((N, Hq), -np.inf)
+    if P == 0 or N == 0:
+        return out, lse
+    import torch
+    rows = max(1, (1 << 22) // max(P, 1))  # query tokens per block (~32 MB of scores per head)
+    keys = torch.arange(P)
+    qt, kt, vt = (torch.from_numpy(np.ascontiguousarray(a)) for a in (q, k, v))
+    for h in range(Hk):
+        kh, vh = kt[:, h, :], vt[:, h, :]
+        for n0 in range(0, N, rows):
+            n1 = min(N, n0 + rows)
+            qb = qt[n0:n1, h * G:(h + 1) * G, :].reshape(-1, D)  # [n*G, D]
+            s = (qb @ kh.T).view(n1 - n0, G, P) * scale
+            visible = torch.ones(n1 - n0, P, dtype=torch.bool)
+            if causal:
+                visible &= keys[None, :] <= (torch.arange(n0, n1)[:, None] + (P - N))
+            if kv_start > 0:
+                visible &= keys[None, :] >= kv_start
+            s = s.masked_fill(~visible[:, None, :], -math.inf)
+            m = s.amax(dim=-1, keepdim=True)
+            has = torch.isfinite(m)
+            m_safe = torch.where(has, m, torch.zeros_like(m))
+            p = torch.exp(s - m_safe)
+            l = p.sum(dim=-1, keepdim=True)
+            o = (p.view(-1, P) @ vh).view(n1 - n0, G, D) / torch.where(l > 0, l, torch.ones_like(l))
+            out[n0:n1, h * G:(h + 1) * G] = o.numpy()
+            lse_b = torch.where(has[..., 0],
+                                (m_safe[..., 0] + torch.log(torch.where(l[..., 0] > 0, l[..., 0],
+                                                                        torch.ones_like(l[..., 0]))))
+                                * LOG2E, torch.full_like(l[..., 0], -math.inf))
+            lse[n0:n1, h * G:(h + 1) * G] = lse_b.numpy()
+    return out, lse
 
 
 def merge_state(v, s, v_other, s_other):

@@ -214,6 +214,7 @@ def test_cfg4_batched_serving(cuda_device):
     am = argmax.cpu().numpy()
     ids_c = ids.cpu()
     for r in range(R):
+        sl = slice(r * B * T, (r + 1) * B * T)
         z = logits[r].float().cpu()
         racc, rids, rbranch = OA.verify_accept(z, ids_c[r])
         assert (int(res[r, 0]), int(res[r, 1])) == (racc, rbranch), r

@@ -198,3 +198,34 @@ def torch_masked_sdpa(q, k_new, v_new, k_prefix, v_prefix, causal: bool = True,
         outs.append(o[0].transpose(0, 1))
         lses.append(lse[0].transpose(0, 1))
     return torch.stack(outs), torch.stack(lses)
+
+
+def torch_tree_sdpa(q, k_new, v_new, k_prefix, v_prefix, causal: bool = True,
+                    sm_scale: float | None = None, kv_start: int = 0):
+    """The torch.sdpa masked path for all branches in ONE call (the timed CPU
+    baseline): the B*T block queries attend [prefix | all branches' block
+    tokens] under a [B*T, P + B*T] boolean tree mask -- the prefix from
+    kv_start on, and within the blocks only the query's own branch (causal:
+    its tokens 0..t). Per branch this is what HF sdpa computes for the plain
+    verify forward of generation/verification.py:204-220.
+    Torch CPU tensors q [B, T, Hq, D], k/v_new [B, T, Hk, D], k/v_prefix
+    [P, Hk, D]; returns out [B, T, Hq, D]."""
+    import torch
+    import torch.nn.functional as F
+    B, T, Hq, D = q.shape
+    P, Hk = k_prefix.shape[0], k_prefix.shape[1]
+    scale = D ** -0.5 if sm_scale is None else float(sm_scale)
+    n = B * T
+    mask = torch.zeros(n, P + n, dtype=torch.bool)
+    mask[:, kv_start:P] = True
+    blk = torch.arange(n) // T
+    pos = torch.arange(n) % T
+    same = blk[:, None] == blk[None, :]
+    if causal:
+        same &= pos[None, :] <= pos[:, None]
+    mask[:, P:] = same
+    kk = torch.cat([k_prefix, k_new.reshape(n, Hk, D)], 0).transpose(0, 1).unsqueeze(0)
+    vv = torch.cat([v_prefix, v_new.reshape(n, Hk, D)], 0).transpose(0, 1).unsqueeze(0)
+    qq = q.reshape(n, Hq, D).transpose(0, 1).unsqueeze(0)
+    o = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=scale, enable_gqa=True)
+    return o[0].transpose(0, 1).reshape(B, T, Hq, D)

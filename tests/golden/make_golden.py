@@ -1,7 +1,7 @@
 """Generate the golden fixtures of tests/golden/ by running the reference itself.
 
-Runs only where the reference checkout exists (default /root/reference, or
-$D2SD_REFERENCE); the committed .npz/.json outputs travel, this script does not
+Runs only where a checkout of the reference exists, named by the environment
+variable $D2SD_REFERENCE (the directory holding generation/ and model/); the committed .npz/.json outputs travel, this script does not
 need to. Nothing here is imported by the product or by the GPU tests.
 
 What is executed from the reference (catnanami/D2-SD), unmodified:
@@ -43,7 +43,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("D2SD_REFERENCE", "/root/reference"))
+if "D2SD_REFERENCE" not in os.environ:
+    raise SystemExit("set D2SD_REFERENCE to the reference checkout (generation/, model/)")
+REF = Path(os.environ["D2SD_REFERENCE"])
 sys.path.insert(0, str(REPO))
 
 

@@ -8,17 +8,23 @@
 // tokens, then merge_state_in_place into the level-1 state; the sink rescale
 // out *= sigmoid(lse - sink) follows at generation/verification.py:173-176.
 //
-// One launch covers every branch. 2, 4 or 8 CTAs share each (block, kv head,
-// 128-row tile); each computes the tile's level-2 attention and merges 64, 32
-// or 16 of its rows. Rows are token*G + g, the G query heads of the kv head, so
-// the whole GQA group shares one K/V tile. Thread 0 TMA-loads the Q tile and the block's K
-// and V (128-byte swizzle) and issues S = Q K^T on tcgen05 into TMEM
-// (M=128, N=32 or 64 keys); each thread (= TMEM lane = row) masks (causal,
-// full or a custom bitmask), exponentiates and writes P back to TMEM as
-// 16-bit pairs; thread 0 issues O = P V (A from TMEM, V MN-major). The
-// epilogue reads O from TMEM 32 columns at a time and merges it with every
-// partial state kernel (a) wrote for the row's query tile (or with a dense
-// prefix state), applies the sink factor and stores the row once.
+// The work is small and memory-bound (the level-2 attention of a block is at
+// most 64 keys per row; the merge reads each row's partial states), so this is
+// a high-occupancy SIMT kernel: one launch covers every branch; a CTA of 256
+// threads takes RP (32, 16 or 8) consecutive rows of one (block, kv head),
+// rows being token*G + g for the G query heads of the kv head.
+//   phase 1  the block's K/V of the kv head (only the keys the CTA's rows can
+//            see) are staged in shared memory; each warp computes the level-2
+//            attention of 4 rows, its four 8-lane groups splitting the keys:
+//            scores into shared memory, a warp-wide softmax, then P.V with a
+//            reduce-scatter that leaves each group one row; the normalised row
+//            and its base-2 LSE go to shared memory. Each row's level 2 is
+//            computed once.
+//   phase 2  (after the previous kernel -- kernel (a) -- has completed) each
+//            row's lane groups merge the local state with every partial state
+//            kernel (a) wrote for the row's query tile (or with a dense prefix
+//            state), apply the sink factor and store the row once; with the
+//            fused output exchange the row goes to every rank's buffer.
 #include "common.cuh"
 #include "plan_layout.h"
 
@@ -29,11 +35,18 @@ namespace {
 
 using namespace plan;
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kGroups = kThreads / 8;  // 8-lane groups of the merge
 constexpr int kMaxBlockLen = 64;
-constexpr int kPanelQ = 128 * 128;  // 128 rows x 128 bytes
+constexpr int kMaxRows = 32;           // rows of one CTA (4 per warp in phase 1)
 
 struct SuffixParams {
+  const void* q;
+  int64_t q_st, q_sh;
+  const void* k_local;
+  const void* v_local;
+  int64_t kv_st, kv_sh;
   const int32_t* plan;
   const void* partial;
   const int32_t* prefix_token;
@@ -51,7 +64,8 @@ struct SuffixParams {
   int32_t has_local;
   int32_t block_len, mask_mode, sink_mode;
   int32_t Hq, G;
-  int32_t rows_per_cta;  // merge rows of a CTA: 64, 32 or 16 (128-row tile / parts)
+  int32_t rows_per_cta;  // RP: 32, 16 or 8
+  int32_t rows_per_unit; // rows of one (block, kv head): block_len * G
   float scale_log2;
   // fused output exchange (d2sd_suffix_merge_gather); world == 0: rows go to out
   void* const* peer_out;               // [2][world]: output buffers of each epoch parity
@@ -76,48 +90,37 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-template <int D, int NK>
-struct SCfg {
-  static constexpr int kPanels = D / 64;
-  static constexpr int kPanelKV = NK * 128;
-  static constexpr int kQBytes = 128 * D * 2;
-  static constexpr int kKVBytes = NK * D * 2;
-  static constexpr int kSmemQ = 0;
-  static constexpr int kSmemK = kQBytes;
-  static constexpr int kSmemV = kSmemK + kKVBytes;
-  static constexpr int kSmemBar = kSmemV + kKVBytes;
-  static constexpr int kSmemMeta = kSmemBar + 64;
-  static constexpr int kSmemBytes = kSmemMeta + 64 * 32 + 1024;
-  // the staged local output [64][D + 4] fp32 reuses the Q/K/V region
-  static_assert(64 * (D + 4) * 4 <= kSmemBar, "stage does not fit");
-};
-
 template <typename T>
 struct Fmt;
 template <>
 struct Fmt<__nv_bfloat16> {
-  static constexpr uint32_t kUmma = 1;
   static __device__ __forceinline__ uint32_t pack(float a, float b) { return pack_bf16x2(a, b); }
+  // the 8 elements of a 16-byte vector as floats
+  static __device__ __forceinline__ void unpack(const uint4& v, float (&f)[8]) {
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      f[2 * k] = __uint_as_float(u[k] << 16);
+      f[2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+    }
+  }
 };
 template <>
 struct Fmt<__half> {
-  static constexpr uint32_t kUmma = 0;
   static __device__ __forceinline__ uint32_t pack(float a, float b) {
     __half2 v = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&v);
   }
-};
-
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (ok) {
-    while (!mbar_try_wait(bar, parity)) {
+  static __device__ __forceinline__ void unpack(const uint4& v, float (&f)[8]) {
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+      f[2 * k] = x.x;
+      f[2 * k + 1] = x.y;
     }
   }
-  return ok != 0;
-}
+};
 
 // Per merge row, written by phase 1, read by phase 2.
 struct RowMeta {
@@ -130,47 +133,71 @@ struct RowMeta {
   int32_t pad[2];
 };
 
-template <typename T, int D, int NK>
-__global__ void __launch_bounds__(kThreads, 1)
-    suffix_attention_kernel(const __grid_constant__ CUtensorMap tm_q,
-                            const __grid_constant__ CUtensorMap tm_k,
-                            const __grid_constant__ CUtensorMap tm_v, const SuffixParams p) {
-  using C = SCfg<D, NK>;
+// Shared memory of a CTA (bytes from a 16-byte aligned base): the block's K
+// and V rows [keys][D], the scores / probabilities of phase 1 [warp][key][4
+// rows], the normalised local outputs [RP][D + 4] fp32 and the row metadata.
+struct SmemLayout {
+  int k, v, p, stage, meta, total;
+  __host__ __device__ SmemLayout(int keys, int D, int elem) {
+    k = 0;
+    v = k + keys * D * elem;
+    p = v + keys * D * elem;
+    stage = p + kWarps * kMaxBlockLen * 16;
+    meta = stage + kMaxRows * (D + 4) * 4;
+    total = meta + kMaxRows * static_cast<int>(sizeof(RowMeta));
+  }
+};
+
+__device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int o) {
+  return __shfl_xor_sync(0xffffffffu, static_cast<unsigned long long>(v), o);
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kThreads, 2) suffix_merge_kernel(const SuffixParams p) {
+  constexpr int NC = D / 64;  // 64-column chunks of a row
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int TB = p.block_len, G = p.G, RP = p.rows_per_cta;
+  const int blk = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * RP;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const SmemLayout sl(p.has_local ? TB : 0, D, static_cast<int>(sizeof(T)));
+  float4* pbuf = reinterpret_cast<float4*>(smem + sl.p);
+  float* stage = reinterpret_cast<float*>(smem + sl.stage);
+  RowMeta* meta = reinterpret_cast<RowMeta*>(smem + sl.meta);
   constexpr int SP = D + 4;  // padded fp32 row of the staged local output
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSmemBar);  // load, S, O
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
-  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  RowMeta* meta = reinterpret_cast<RowMeta*>(smem + C::kSmemMeta);
-  float* stage = reinterpret_cast<float*>(smem + C::kSmemQ);  // reuses Q after the MMAs
-
-  const int blk = blockIdx.x, h = blockIdx.y;
-  // 128-row tile rt, merge part `part` = rows [part*RP, part*RP + RP) of it
-  const int RP = p.rows_per_cta;
-  const int parts = kTileRows / RP;
-  const int rt = blockIdx.z / parts, part = blockIdx.z - (blockIdx.z / parts) * parts;
-  const int TB = p.block_len, G = p.G;
-  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const float sl2 = p.scale_log2;
-
-  // ---- phase 1a: level-2 attention on tcgen05 (warps 0-3, thread = row) ----
-  uint32_t tmem = 0;
-  bool ok = true;
-  float lse_l = -INFINITY, inv_l = 0.f;
-  const int row = threadIdx.x & 127;  // TMEM lane of warps 0-3
-  const int R = rt * 128 + row;
-  const int t = R / G, g = R - (R / G) * G;
-  const bool valid = t < TB;
-  const int tok = blk * TB + t;
   // the next kernel may set itself up now; it waits for this one to complete
   grid_dep_launch();
-  // ---- row metadata of this CTA's merge rows, from the (static) plan: warps
-  // 4-5, idle during the level-2 attention, so the lookups overlap it ----
-  if ((warp == 4 || warp == 5) && threadIdx.x - 128 < RP) {
-    const int lr = threadIdx.x - 128;
-    const int Rm = rt * 128 + RP * part + lr;
+
+  // keys the CTA's rows can see: a causal row of token t sees keys 0..t
+  const int t_last = min(TB - 1, (r0 + RP - 1) / G);
+  const int nkeys =
+      !p.has_local ? 0 : (p.mask_mode == D2SD_MASK_CAUSAL ? t_last + 1 : TB);
+
+  // ---- the block's K/V rows of this kv head into shared memory (loads first,
+  // then the row metadata while they are in flight, then the stores) ----
+  constexpr int VR = D * static_cast<int>(sizeof(T)) / 16;  // 16-byte vectors per row
+  constexpr int EV = 16 / static_cast<int>(sizeof(T));      // elements per vector
+  const int nvec = nkeys * VR;
+  uint4 kvbuf[4];
+  int kvdst[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int i = threadIdx.x + u * kThreads;
+    kvdst[u] = -1;
+    if (i < 2 * nvec) {
+      const int kv = i >= nvec;
+      const int ii = kv ? i - nvec : i;
+      const int j = ii / VR, c = ii - (ii / VR) * VR;
+      const T* src = static_cast<const T*>(kv ? p.v_local : p.k_local) +
+                     static_cast<int64_t>(blk * TB + j) * p.kv_st +
+                     static_cast<int64_t>(h) * p.kv_sh + c * EV;
+      kvbuf[u] = *reinterpret_cast<const uint4*>(src);
+      kvdst[u] = (kv ? sl.v : sl.k) + ii * 16;
+    }
+  }
+  if (threadIdx.x < RP) {
+    // row metadata from the (static) plan: the partial slots of the row's query tile
+    const int lr = threadIdx.x;
+    const int Rm = r0 + lr;
     const int tm = Rm / G, gm = Rm - (Rm / G) * G;
     const bool vm = tm < TB;
     const int tokm = blk * TB + tm;
@@ -189,160 +216,198 @@ __global__ void __launch_bounds__(kThreads, 1)
         prow = qrow % kTileRows;
       }
     }
-    // lse_local is written by the warps that own the row's TMEM lane
+    meta[lr].lse_local = -INFINITY;
     meta[lr].tok = vm ? tokm : -1;
     meta[lr].hq = h * G + gm;
     meta[lr].slot = slot;
     meta[lr].nslots = nslots;
     meta[lr].prow = prow;
   }
-  if (p.has_local) {
-    if (threadIdx.x == 0) {
-      for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
-      *abort = 0;
-      fence_mbar_init();
-      fence_proxy_async_smem();
-    }
-    if (warp == 0) {
-      tmem_alloc(tmem_slot, 256);
-      tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    tmem = *tmem_slot;
-    if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(&bars[0], C::kQBytes + 2 * C::kKVBytes);
 #pragma unroll
-      for (int pn = 0; pn < C::kPanels; ++pn) {
-        tma_load_3d(smem + C::kSmemQ + pn * kPanelQ, &tm_q, &bars[0], pn * 64, h * G,
-                    blk * TB + rt * (128 / G));
-        tma_load_3d(smem + C::kSmemK + pn * C::kPanelKV, &tm_k, &bars[0], pn * 64, h, blk * TB);
-        tma_load_3d(smem + C::kSmemV + pn * C::kPanelKV, &tm_v, &bars[0], pn * 64, h, blk * TB);
-      }
-      if (mbar_wait(&bars[0], 0, abort)) {
-        tc_fence_after();
-        constexpr uint32_t idesc = umma_idesc(128, NK, false, Fmt<T>::kUmma);
-        const uint32_t a0 = smem_u32(smem + C::kSmemQ);
-        const uint32_t b0 = smem_u32(smem + C::kSmemK);
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t ka = (ks / 4) * kPanelQ + (ks % 4) * 32;
-          const uint32_t kb = (ks / 4) * C::kPanelKV + (ks % 4) * 32;
-          umma_ss(tmem, umma_desc_sw128(a0 + ka, 16, 1024), umma_desc_sw128(b0 + kb, 16, 1024),
-                  idesc, ks > 0 ? 1u : 0u);
-        }
-        umma_commit(&bars[1]);
-      }
-    }
-    if (warp < 4) {
-      const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-      ok = warp_wait(&bars[1], 0, abort);
-      if (ok) {
-        tc_fence_after();
-        uint32_t s[NK];
-        tmem_ld32_wait(lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-        if (NK == 64)
-          tmem_ld32_wait(lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 % NK]));
-        uint64_t allowed = 0;
-        if (valid) {
-          if (p.mask_mode == D2SD_MASK_CAUSAL) allowed = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
-          else if (p.mask_mode == D2SD_MASK_CUSTOM) allowed = p.custom_mask[tok];
-          else allowed = ~0ull;
-          if (TB < 64) allowed &= (1ull << TB) - 1ull;
-        }
-        float m = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < NK; ++j) {
-          if (!((allowed >> j) & 1ull)) s[j] = 0xff800000u;
-          m = fmaxf(m, __uint_as_float(s[j]));
-        }
-        const float mm = (m == -INFINITY) ? 0.f : m * sl2;
-        float l = 0.f;
-#pragma unroll
-        for (int c = 0; c < NK / 32; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, -mm));
-            const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, -mm));
-            l += p0 + p1;
-            pk[e] = Fmt<T>::pack(p0, p1);
-          }
-          tmem_st16(lane_base + c * 16, pk);
-        }
-        tmem_st_wait();
-        if (l > 0.f) {
-          lse_l = mm + fast_log2(l);
-          inv_l = 1.f / l;
-        }
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (threadIdx.x == 0 && !*abort) {
-      tc_fence_after();
-      constexpr uint32_t idesc = umma_idesc(128, D, true, Fmt<T>::kUmma);
-      const uint32_t b0 = smem_u32(smem + C::kSmemV);
-#pragma unroll
-      for (int ks = 0; ks < NK / 16; ++ks) {
-        umma_ts(tmem + 128, tmem + ks * 8, umma_desc_sw128(b0 + ks * 16 * 128, C::kPanelKV, 1024),
-                idesc, ks > 0 ? 1u : 0u);
-      }
-      umma_commit(&bars[2]);
-    }
-    if (warp < 4) {
-      ok = warp_wait(&bars[2], 0, abort) && ok;
-      tc_fence_after();
-    }
+  for (int u = 0; u < 4; ++u)
+    if (kvdst[u] >= 0) *reinterpret_cast<uint4*>(smem + kvdst[u]) = kvbuf[u];
+  for (int i = threadIdx.x + 4 * kThreads; i < 2 * nvec; i += kThreads) {  // block_len > 32 at D 128
+    const int kv = i >= nvec;
+    const int ii = kv ? i - nvec : i;
+    const int j = ii / VR, c = ii - (ii / VR) * VR;
+    const T* src = static_cast<const T*>(kv ? p.v_local : p.k_local) +
+                   static_cast<int64_t>(blk * TB + j) * p.kv_st + static_cast<int64_t>(h) * p.kv_sh +
+                   c * EV;
+    *reinterpret_cast<uint4*>(smem + (kv ? sl.v : sl.k) + ii * 16) =
+        *reinterpret_cast<const uint4*>(src);
   }
-
-  // ---- phase 1b: this CTA's merge rows: local O -> smem ----
-  // warp w (< 4) owns TMEM lanes [32w, 32w + 32); it takes part if those lanes
-  // meet the CTA's rows [RP*part, RP*part + RP)
-  if (warp < 4 && warp * 32 < RP * (part + 1) && warp * 32 + 32 > RP * part) {
-    const int lr = row - RP * part;
-    const bool mine = lr >= 0 && lr < RP;
-    if (mine) meta[lr].lse_local = (p.has_local && ok) ? lse_l : -INFINITY;
-    if (p.has_local) {
-      const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-      const float sc = ok ? inv_l : 0.f;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32_wait(lane_base + 128 + c * 32, o);
-        if (!mine) continue;
-        float4* dst = reinterpret_cast<float4*>(stage + lr * SP + c * 32);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          dst[e] = make_float4(__uint_as_float(o[4 * e]) * sc, __uint_as_float(o[4 * e + 1]) * sc,
-                               __uint_as_float(o[4 * e + 2]) * sc,
-                               __uint_as_float(o[4 * e + 3]) * sc);
-      }
-    }
-  }
-  if (p.has_local) tc_fence_before();
   __syncthreads();
-  if (p.has_local && warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 256);
-  }
-  if (p.has_local && threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
 
-  // ---- phase 2: merge. The CTA's 64 lane groups of 8 lanes (4 per warp) are
-  // spread over its RP rows, GS = 64 / RP groups per row (in the same warp); a
+  // ---- phase 1: level-2 attention, 4 rows per warp. Lane j8 of 8-lane group
+  // gi holds columns {c*64 + 8*j8 + e}; for the scores and P.V the groups split
+  // the keys (group gi takes keys gi, gi+4, ...) ----
+  if (p.has_local && warp * 4 < RP) {
+    const int gi = lane >> 3, j8 = lane & 7;
+    const float sl2 = p.scale_log2;
+    uint64_t allowed[4];
+    uint64_t qf[4][NC * 4];  // the rows' q at this lane's columns, fp32 pairs
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int R = r0 + 4 * warp + r;
+      const int t = R / G, g = R - (R / G) * G;
+      const bool valid = t < TB;
+      const int tok = blk * TB + t;
+      uint64_t m = 0;
+      if (valid) {
+        if (p.mask_mode == D2SD_MASK_CAUSAL) m = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
+        else if (p.mask_mode == D2SD_MASK_CUSTOM) m = p.custom_mask[tok];
+        else m = ~0ull;
+        if (TB < 64) m &= (1ull << TB) - 1ull;
+      }
+      allowed[r] = m;
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+        if (valid)
+          raw = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
+                                                static_cast<int64_t>(tok) * p.q_st +
+                                                static_cast<int64_t>(h * G + g) * p.q_sh +
+                                                c * 64 + 8 * j8);
+        float f[8];
+        Fmt<T>::unpack(raw, f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) qf[r][c * 4 + k] = f2_pack(f[2 * k], f[2 * k + 1]);
+      }
+    }
+    float4* pw = pbuf + warp * kMaxBlockLen;  // [key] -> the 4 rows' scores, then probabilities
+    const int iters = (nkeys + 3) / 4;
+    for (int it = 0; it < iters; ++it) {
+      const int j = gi + 4 * it;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      if (j < nkeys) {
+        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const uint4 kk = *reinterpret_cast<const uint4*>(
+              smem + sl.k + (static_cast<int>(j) * D + c * 64 + 8 * j8) * static_cast<int>(sizeof(T)));
+          float kf[8];
+          Fmt<T>::unpack(kk, kf);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t k2 = f2_pack(kf[2 * k], kf[2 * k + 1]);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[r] = f2_fma(qf[r][c * 4 + k], k2, acc[r]);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float x, y;
+          f2_unpack(acc[r], x, y);
+          d[r] = x + y;
+        }
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) d[r] += __shfl_xor_sync(0xffffffffu, d[r], o);
+      if (j8 == 0 && j < nkeys) {
+        float4 s;
+        s.x = ((allowed[0] >> j) & 1ull) ? d[0] * sl2 : -INFINITY;
+        s.y = ((allowed[1] >> j) & 1ull) ? d[1] * sl2 : -INFINITY;
+        s.z = ((allowed[2] >> j) & 1ull) ? d[2] * sl2 : -INFINITY;
+        s.w = ((allowed[3] >> j) & 1ull) ? d[3] * sl2 : -INFINITY;
+        pw[j] = s;
+      }
+    }
+    __syncwarp();
+    // softmax of the 4 rows over the keys: lane L holds keys L and L + 32
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    float4 sa = lane < nkeys ? pw[lane] : ninf;
+    float4 sb = lane + 32 < nkeys ? pw[lane + 32] : ninf;
+    float m[4] = {fmaxf(sa.x, sb.x), fmaxf(sa.y, sb.y), fmaxf(sa.z, sb.z), fmaxf(sa.w, sb.w)};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], o));
+#pragma unroll
+    for (int r = 0; r < 4; ++r) m[r] = (m[r] == -INFINITY) ? 0.f : m[r];
+    sa = make_float4(fast_exp2(sa.x - m[0]), fast_exp2(sa.y - m[1]), fast_exp2(sa.z - m[2]),
+                     fast_exp2(sa.w - m[3]));
+    sb = make_float4(fast_exp2(sb.x - m[0]), fast_exp2(sb.y - m[1]), fast_exp2(sb.z - m[2]),
+                     fast_exp2(sb.w - m[3]));
+    float l[4] = {sa.x + sb.x, sa.y + sb.y, sa.z + sb.z, sa.w + sb.w};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) l[r] += __shfl_xor_sync(0xffffffffu, l[r], o);
+    if (lane < nkeys) pw[lane] = sa;
+    if (lane + 32 < nkeys) pw[lane + 32] = sb;
+    __syncwarp();
+    // this group's row (gi) after the reduce-scatter below
+    const float l_g = gi == 0 ? l[0] : gi == 1 ? l[1] : gi == 2 ? l[2] : l[3];
+    const float m_g = gi == 0 ? m[0] : gi == 1 ? m[1] : gi == 2 ? m[2] : m[3];
+    const float inv_g = l_g > 0.f ? 1.f / l_g : 0.f;
+    const int lr_g = 4 * warp + gi;
+    // P.V, 64 columns at a time
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      uint64_t o[4][4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[r][k] = 0ull;
+      for (int it = 0; it < iters; ++it) {
+        const int j = gi + 4 * it;
+        if (j >= nkeys) break;
+        const float4 pj = pw[j];
+        const uint4 vv = *reinterpret_cast<const uint4*>(
+            smem + sl.v + (j * D + c * 64 + 8 * j8) * static_cast<int>(sizeof(T)));
+        float vf[8];
+        Fmt<T>::unpack(vv, vf);
+        const uint64_t p2[4] = {f2_pack(pj.x, pj.x), f2_pack(pj.y, pj.y), f2_pack(pj.z, pj.z),
+                                f2_pack(pj.w, pj.w)};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t v2 = f2_pack(vf[2 * k], vf[2 * k + 1]);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) o[r][k] = f2_fma(p2[r], v2, o[r][k]);
+        }
+      }
+      // reduce-scatter over the four groups: group gi ends with row gi
+      const bool hi = (gi & 2) != 0, lo = (gi & 1) != 0;
+      uint64_t res[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint64_t keep0 = hi ? o[2][k] : o[0][k], send0 = hi ? o[0][k] : o[2][k];
+        uint64_t keep1 = hi ? o[3][k] : o[1][k], send1 = hi ? o[1][k] : o[3][k];
+        keep0 = f2_add(keep0, shfl_xor_u64(send0, 16));
+        keep1 = f2_add(keep1, shfl_xor_u64(send1, 16));
+        const uint64_t keep = lo ? keep1 : keep0, send = lo ? keep0 : keep1;
+        res[k] = f2_add(keep, shfl_xor_u64(send, 8));
+      }
+      if (lr_g < RP) {
+        float* dst = stage + lr_g * SP + c * 64 + 8 * j8;
+        float a0, a1, b0, b1, c0, c1, d0, d1;
+        f2_unpack(res[0], a0, a1);
+        f2_unpack(res[1], b0, b1);
+        f2_unpack(res[2], c0, c1);
+        f2_unpack(res[3], d0, d1);
+        reinterpret_cast<float4*>(dst)[0] = make_float4(a0 * inv_g, a1 * inv_g, b0 * inv_g, b1 * inv_g);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(c0 * inv_g, c1 * inv_g, d0 * inv_g, d1 * inv_g);
+      }
+    }
+    if (j8 == 0 && lr_g < RP) meta[lr_g].lse_local = l_g > 0.f ? m_g + fast_log2(l_g) : -INFINITY;
+  }
+  __syncthreads();
+
+  // ---- phase 2: merge. The CTA's 32 lane groups of 8 lanes (4 per warp) are
+  // spread over its RP rows, GS = 32 / RP groups per row (in the same warp); a
   // group takes every GS-th slot of its row, 8 lanes across the row's columns
   // (D/8 each), with up to 8 slot rows and all their LSEs in flight before any
-  // use; the row's groups then add their partial sums with shuffles ----
-  // the partial slots come from the previous kernel (kernel (a)): wait for it.
-  // Phase 1 reads only q and the block's K/V, which precede kernel (a).
+  // use; the row's groups then add their partial sums with shuffles.
+  // The partial slots come from the previous kernel (kernel (a)): wait for it.
+  // Phase 1 read only q and the block's K/V, which precede kernel (a).
   grid_dep_wait();
   constexpr int CPL = D / 8;          // columns per lane
   constexpr int VEC = CPL * 2 / 16;   // 16-byte vectors per lane and slot row
   constexpr int kBatch = 8;           // slot rows in flight per lane
   constexpr int kLseBlocks = 4;       // LSE blocks of 8 slots loaded together
-  static_assert(kThreads / 32 * 4 == 64, "16 warps x 4 lane groups");
-  const int GS = 64 / RP;             // lane groups per row: 1, 2 or 4
+  const int GS = kGroups / RP;        // lane groups per row: 1, 2 or 4
   const int64_t sbytes = slot_bytes(D);
   const uint8_t* part_base = static_cast<const uint8_t*>(p.partial);
   const int gi = warp * 4 + (lane >> 3), j8 = lane & 7;
@@ -504,6 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (j8 == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
   }
+
   if (p.world > 0) {
     // Arrival. Every CTA makes its peer stores visible system-wide and takes a
     // ticket; the CTA that takes the last one signals every rank once (one
@@ -551,42 +617,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <typename T, int D, int NK>
-int launch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                  const SuffixParams& prm, dim3 grid, cudaStream_t stream) {
-  using C = SCfg<D, NK>;
-  static int configured = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured != dev) {
-    cudaError_t e = cudaFuncSetAttribute(suffix_attention_kernel<T, D, NK>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::kSmemBytes);
-    // the shared-memory carve-out kernel (a) runs with: no reconfiguration of
-    // the SMs between the two kernels
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(suffix_attention_kernel<T, D, NK>,
-                               cudaFuncAttributePreferredSharedMemoryCarveout,
-                               cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess)
-      return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    configured = dev;
-  }
-  return launch_pdl(suffix_attention_kernel<T, D, NK>, grid, dim3(kThreads), C::kSmemBytes, stream,
-                    "suffix_attention_kernel", tq, tk, tv, prm);
-}
-
-template <typename T>
-int dispatch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                    const SuffixParams& prm, int D, int NK, dim3 grid, cudaStream_t st) {
-  if (D == 128) {
-    return NK == 32 ? launch_suffix<T, 128, 32>(tq, tk, tv, prm, grid, st)
-                    : launch_suffix<T, 128, 64>(tq, tk, tv, prm, grid, st);
-  }
-  return NK == 32 ? launch_suffix<T, 64, 32>(tq, tk, tv, prm, grid, st)
-                  : launch_suffix<T, 64, 64>(tq, tk, tv, prm, grid, st);
-}
-
 // ---------------------------------------------------------------------------
 // merge_state_in_place: (v, s) <- merge((v, s), (v_other, s_other)), base-2.
 // Reference: flashinfer.merge_state_in_place at model/cascade_graph.py:58-60.
@@ -626,15 +656,31 @@ __global__ void merge_state_kernel(T* v, int64_t v_st, int64_t v_sh, float* s, i
 
 namespace d2sd {
 namespace {
-// Merge parts per 128-row tile (64, 32 or 16 rows per CTA): more CTAs, and
-// more lanes per row, when few tiles would leave most SMs idle (KV-head
-// sharding over several GPUs leaves each with few heads, and each query tile
-// then has many partial slots to merge).
-int merge_parts(int64_t tiles) {
-  const int64_t sms = current_sm_count();
-  int parts = 2;
-  while (parts < 8 && tiles * parts * 2 <= sms) parts *= 2;
-  return parts;
+// Rows per CTA (32, 16 or 8): fewer, and more lane groups per row, when few
+// rows would leave most SMs idle (KV-head sharding over several GPUs leaves
+// each rank few heads, and each query tile then has many partial slots).
+int rows_per_cta(int64_t rows) {
+  const int64_t target = 2 * static_cast<int64_t>(current_sm_count());
+  int rp = kMaxRows;
+  while (rp > 8 && (rows + rp - 1) / rp < target) rp /= 2;
+  return rp;
+}
+
+template <typename T, int D>
+int launch_suffix(const SuffixParams& prm, dim3 grid, int smem, cudaStream_t stream) {
+  static int configured = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    cudaError_t e = cudaFuncSetAttribute(suffix_merge_kernel<T, D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         SmemLayout(kMaxBlockLen, D, sizeof(T)).total);
+    if (e != cudaSuccess)
+      return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured = dev;
+  }
+  return launch_pdl(suffix_merge_kernel<T, D>, grid, dim3(kThreads), smem, stream,
+                    "suffix_merge_kernel", prm);
 }
 
 struct PeerArgs {
@@ -643,19 +689,18 @@ struct PeerArgs {
   int32_t world = 0, rank = 0, head_offset = 0;
   int64_t st = 0, sh = 0, epoch = 0;
 };
+
 int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head,
-                                 const void* k_local, const void* v_local, int64_t kv_stride_token,
-                                 int64_t kv_stride_head, int32_t num_blocks, int32_t block_len,
-                                 int32_t mask_mode, const uint64_t* custom_mask,
-                                 const void* partial, const int32_t* plan,
-                                 const int32_t* prefix_token, const void* prefix_out,
-                                 int64_t prefix_out_stride_token, int64_t prefix_out_stride_head,
-                                 const float* prefix_lse, int64_t prefix_lse_stride_token,
-                                 void* out, int64_t out_stride_token, int64_t out_stride_head,
-                                 float* lse, int64_t lse_stride_token, const float* sinks,
-                                 int32_t sink_mode, int32_t num_qo_heads, int32_t num_kv_heads,
-                                 int32_t head_dim, int32_t dtype, float sm_scale,
-                                 int32_t* status, void* stream, const PeerArgs& pa) {
+                      const void* k_local, const void* v_local, int64_t kv_stride_token,
+                      int64_t kv_stride_head, int32_t num_blocks, int32_t block_len,
+                      int32_t mask_mode, const uint64_t* custom_mask, const void* partial,
+                      const int32_t* plan, const int32_t* prefix_token, const void* prefix_out,
+                      int64_t prefix_out_stride_token, int64_t prefix_out_stride_head,
+                      const float* prefix_lse, int64_t prefix_lse_stride_token, void* out,
+                      int64_t out_stride_token, int64_t out_stride_head, float* lse,
+                      int64_t lse_stride_token, const float* sinks, int32_t sink_mode,
+                      int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                      float sm_scale, int32_t* status, void* stream, const PeerArgs& pa) {
   if (!out || num_blocks < 0 || block_len <= 0 || num_qo_heads <= 0 || num_kv_heads <= 0 ||
       num_qo_heads % num_kv_heads != 0)
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: invalid argument");
@@ -685,8 +730,21 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: out rows must be 16-byte aligned");
   if (partial && (reinterpret_cast<uintptr_t>(partial) & 15u))
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: partial must be 16-byte aligned");
+  if (k_local && (!aligned16(q) || !aligned16(k_local) || !aligned16(v_local) ||
+                  q_stride_token % 8 || q_stride_head % 8 || kv_stride_token % 8 ||
+                  kv_stride_head % 8))
+    return fail(D2SD_ERR_INVALID_ARGUMENT,
+                "d2sd_suffix_merge: q/k/v must be 16-byte aligned with strides multiple of 8");
 
   SuffixParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  prm.q = q;
+  prm.q_st = q_stride_token;
+  prm.q_sh = q_stride_head;
+  prm.k_local = k_local;
+  prm.v_local = v_local;
+  prm.kv_st = kv_stride_token;
+  prm.kv_sh = kv_stride_head;
   prm.plan = plan;
   prm.partial = partial;
   prm.prefix_token = prefix_token;
@@ -718,58 +776,29 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
   prm.pg_sh = pa.sh;
   prm.epoch = pa.epoch;
 
-  CUtensorMap tq, tk, tv;
-  std::memset(&tq, 0, sizeof(tq));
-  std::memset(&tk, 0, sizeof(tk));
-  std::memset(&tv, 0, sizeof(tv));
-  dim3 grid;
-  int NK = 32;
-  if (k_local) {
-    prm.block_len = block_len;
-    NK = block_len <= 32 ? 32 : 64;
-    const CUtensorMapDataType tdt =
-        dtype == D2SD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if (!aligned16(q) || !aligned16(k_local) || !aligned16(v_local) || q_stride_token % 8 ||
-        q_stride_head % 8 || kv_stride_token % 8 || kv_stride_head % 8)
-      return fail(D2SD_ERR_INVALID_ARGUMENT,
-                  "d2sd_suffix_merge: q/k/v must be 16-byte aligned with strides multiple of 8");
-    const uint64_t ntok = static_cast<uint64_t>(num_blocks) * block_len;
-    {
-      const uint64_t dims[3] = {static_cast<uint64_t>(head_dim),
-                                static_cast<uint64_t>(num_qo_heads), ntok};
-      const uint64_t str[2] = {static_cast<uint64_t>(q_stride_head) * 2,
-                               static_cast<uint64_t>(q_stride_token) * 2};
-      const uint32_t box[3] = {64, static_cast<uint32_t>(G), static_cast<uint32_t>(128 / G)};
-      int rc = encode_tensor_map(&tq, tdt, q, 3, dims, str, box, "q");
-      if (rc) return rc;
-    }
-    {
-      const uint64_t dims[3] = {static_cast<uint64_t>(head_dim),
-                                static_cast<uint64_t>(num_kv_heads), ntok};
-      const uint64_t str[2] = {static_cast<uint64_t>(kv_stride_head) * 2,
-                               static_cast<uint64_t>(kv_stride_token) * 2};
-      const uint32_t box[3] = {64, 1, static_cast<uint32_t>(NK)};
-      int rc = encode_tensor_map(&tk, tdt, k_local, 3, dims, str, box, "k_local");
-      if (rc) return rc;
-      rc = encode_tensor_map(&tv, tdt, v_local, 3, dims, str, box, "v_local");
-      if (rc) return rc;
-    }
-    const int64_t base = static_cast<int64_t>(num_blocks) * num_kv_heads * ((block_len * G + 127) / 128);
-    const int parts = merge_parts(base);
-    prm.rows_per_cta = plan::kTileRows / parts;
-    grid = dim3(num_blocks, num_kv_heads, static_cast<unsigned>(parts * ((block_len * G + 127) / 128)));
-  } else {
-    // no level 2: the blocks do not matter, tile all tokens of a head together
-    const int64_t ntok = static_cast<int64_t>(num_blocks) * block_len;
-    prm.block_len = static_cast<int32_t>(ntok);
-    const int64_t tiles = (ntok * G + 127) / 128;
-    const int parts = merge_parts(static_cast<int64_t>(num_kv_heads) * tiles);
-    prm.rows_per_cta = plan::kTileRows / parts;
-    grid = dim3(1, num_kv_heads, static_cast<unsigned>(parts * tiles));
+  // a unit is one (block, kv head): block_len * G rows; without level 2 the
+  // blocks do not matter and all tokens of a head form one unit
+  int64_t units_x = num_blocks, tb = block_len;
+  if (!k_local) {
+    tb = static_cast<int64_t>(num_blocks) * block_len;
+    units_x = 1;
   }
+  if (tb * G > INT32_MAX / 2)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: too many tokens");
+  prm.block_len = static_cast<int32_t>(tb);
+  prm.rows_per_unit = static_cast<int32_t>(tb * G);
+  const int rp = rows_per_cta(units_x * num_kv_heads * tb * G);
+  prm.rows_per_cta = rp;
+  const dim3 grid(static_cast<unsigned>(units_x), static_cast<unsigned>(num_kv_heads),
+                  static_cast<unsigned>((tb * G + rp - 1) / rp));
+  const int esz = 2;  // bf16 or f16
+  const int smem = SmemLayout(k_local ? static_cast<int>(tb) : 0, head_dim, esz).total;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dtype == D2SD_DTYPE_BF16) return dispatch_suffix<__nv_bfloat16>(tq, tk, tv, prm, head_dim, NK, grid, st);
-  return dispatch_suffix<__half>(tq, tk, tv, prm, head_dim, NK, grid, st);
+  if (dtype == D2SD_DTYPE_BF16)
+    return head_dim == 128 ? launch_suffix<__nv_bfloat16, 128>(prm, grid, smem, st)
+                           : launch_suffix<__nv_bfloat16, 64>(prm, grid, smem, st);
+  return head_dim == 128 ? launch_suffix<__half, 128>(prm, grid, smem, st)
+                         : launch_suffix<__half, 64>(prm, grid, smem, st);
 }
 }  // namespace
 }  // namespace d2sd

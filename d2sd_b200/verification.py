@@ -12,6 +12,12 @@ kernel (b) for the per-branch causal attention, the LSE merge and, for GPT-OSS,
 the sink rescale (:152-176). The GPT-OSS sliding layers see the last
 `sliding_window` prefix keys, as in the reference (:130-135).
 
+``past_key_values`` is the reference's DynamicCache or a ``PagedKVCache``
+holding the same prefix (its ``length`` positions of every layer); with the
+paged cache the whole D3 step -- this forward, ``verify`` and
+``PagedKVCache.commit`` -- runs without the reference's per-step
+reallocation of the cache.
+
 ``cascade_graph_runner`` is accepted for call compatibility; the fused kernel
 (b) already does what the runner's graph did.
 """
@@ -23,11 +29,20 @@ import torch
 
 from . import ops
 from .cascade import CascadePlan, Request, cascade_attention
+from .kv_cache import PagedKVCache
 
 
-def _layer_kv(past_key_values, idx):
+def _prefix(past_key_values, idx):
+    """(k, v, kv_layout, prefix length, page table) of layer idx. A
+    ``PagedKVCache`` is read through its page table (the D3 loop then commits
+    the accepted rows with ``PagedKVCache.commit`` instead of the reference's
+    torch.cat, generation/d3_generator.py:227-232); a DynamicCache layer
+    [1, Hk, P, D] is read in place as an HND tensor."""
+    if isinstance(past_key_values, PagedKVCache):
+        c = past_key_values
+        return c.k[idx], c.v[idx], c.kv_layout, c.length, c.page_table
     layer = past_key_values.layers[idx]
-    return layer.keys, layer.values
+    return layer.keys[0], layer.values[0], "hnd", layer.keys.shape[2], None
 
 
 @torch.no_grad()
@@ -67,8 +82,7 @@ def cascade_verify_forward(target_model, input_ids: torch.Tensor, position_ids: 
         v_new = v_new.transpose(1, 2)
         new_kv_list.append((k_new, v_new))
 
-        keys, values = _layer_kv(past_key_values, layer_idx)  # [1, Hk, P, D]
-        P = keys.shape[2]
+        keys, values, kv_layout, P, page_table = _prefix(past_key_values, layer_idx)
         window = getattr(attn, "sliding_window", None)
         kv_start = P - window if (window is not None and P > window) else 0
         key = (P, kv_start, Hq, Hk, D)
@@ -78,8 +92,8 @@ def cascade_verify_forward(target_model, input_ids: torch.Tensor, position_ids: 
             plans[key] = plan
         sinks = attn.sinks.float() if is_gpt_oss else None
         out, _ = cascade_attention(q.transpose(1, 2), k_new.transpose(1, 2),
-                                   v_new.transpose(1, 2), keys[0], values[0], "hnd", P,
-                                   causal=True, sm_scale=D ** -0.5,
+                                   v_new.transpose(1, 2), keys, values, kv_layout, P,
+                                   page_table=page_table, causal=True, sm_scale=D ** -0.5,
                                    sliding_window=None if kv_start == 0 else P - kv_start,
                                    sinks=sinks, sink_mode="reference", plan=plan)
         hidden = residual + attn.o_proj(out.reshape(bsz, seq_len, -1))

@@ -34,9 +34,10 @@ def tiny(kind, dev):
     return m.to(dev).to(torch.bfloat16).eval()
 
 
-def oracle_forward(model, ids, pos, cache, is_gpt_oss):
+def oracle_forward(model, ids, pos, cache, is_gpt_oss, new_kv=None):
     """The reference's layer loop (generation/verification.py:96-201) with the
-    attention computed by the float64 oracle of the same cascade."""
+    attention computed by the float64 oracle of the same cascade; appends each
+    layer's post-RoPE (k, v) [B, Hk, T, D] to ``new_kv`` when given."""
     from oracle import rope as OR
     m = model.model
     B, T = ids.shape
@@ -56,6 +57,8 @@ def oracle_forward(model, ids, pos, cache, is_gpt_oss):
                                gpt_oss=is_gpt_oss)
         q, k = q.transpose(1, 2), k.transpose(1, 2)
         v = v.transpose(1, 2)
+        if new_kv is not None:
+            new_kv.append((k, v))
         kp = cache.layers[li].keys[0].transpose(0, 1)
         vp = cache.layers[li].values[0].transpose(0, 1)
         sw = getattr(at, "sliding_window", None)
@@ -100,3 +103,68 @@ def test_cascade_verify_forward_matches_oracle(cuda_device, kind):
     assert err <= 2e-2 * scale + 2e-2, (err, scale)
     agree = (logits.argmax(-1) == ref.argmax(-1)).float().mean().item()
     assert agree > 0.95
+
+
+def test_d3_loop_on_the_paged_cache(cuda_device):
+    """Three D3 steps (generation/d3_generator.py:186-239): verify forward ->
+    acceptance -> commit -> next block at the advanced positions, run on the
+    paged cache with the kernels, beside the reference loop (DynamicCache +
+    torch.cat commit) with the float64 oracle as its attention, fed the same
+    commits. Each step: logits within tolerance, acceptance bit-exact against
+    the oracle walk of the same logits, and the paged cache equal to the
+    reference's concatenated cache bit for bit."""
+    from transformers import DynamicCache
+
+    import d2sd_b200 as d
+    from oracle import accept as OA
+    dev = cuda_device
+    model = tiny("qwen3", dev)
+    nl = len(model.model.layers)
+    Hk, D = model.config.num_key_value_heads, model.model.layers[0].self_attn.head_dim
+    g = torch.Generator().manual_seed(5)
+    P, B, T, steps = 300, 4, 16, 3
+    prompt = torch.randint(0, 512, (1, P), generator=g).to(dev)
+    ref_cache = DynamicCache()
+    with torch.no_grad():
+        model(prompt, past_key_values=ref_cache, use_cache=True)
+    paged = d.PagedKVCache(nl, Hk, D, P + steps * T + 16, device=dev,
+                           page_order=torch.randperm(-(-(P + steps * T + 16) // 16), generator=g))
+    for l in range(nl):
+        paged.write(l, ref_cache.layers[l].keys[0].transpose(0, 1),
+                    ref_cache.layers[l].values[0].transpose(0, 1))
+    paged.length = P
+    ver = d.Verifier(B, T, 512, dev)
+    anchor = int(prompt[0, -1])
+    for step in range(steps):
+        L0 = paged.length
+        pos = torch.arange(L0, L0 + T, device=dev).unsqueeze(0)
+        block = torch.randint(0, 512, (B, T), generator=g).to(dev)
+        block[:, 0] = anchor
+        # drafts that agree with the target for a few positions (first pass)
+        first, _, _ = d.cascade_verify_forward(model, block, pos, paged, output_hidden_states=False)
+        pred = first.argmax(-1)
+        for b in range(B):
+            block[b, 1:1 + 2 * b] = pred[b, :2 * b]
+        logits, _, new_kv = d.cascade_verify_forward(model, block, pos, paged,
+                                                     output_hidden_states=False)
+        with torch.no_grad():
+            ref = oracle_forward(model, block, pos, copy.deepcopy(ref_cache), False)
+        err = (logits.float() - ref.float()).abs().max().item()
+        assert err <= 2e-2 * ref.float().abs().max().item() + 2e-2, (step, err)
+        ver.launch(logits, block)
+        paged.commit([k for k, _ in new_kv], [v for _, v in new_kv], ver.result)
+        acc, ids, branch = ver.read()
+        racc, rids, rbranch = OA.verify_accept(logits.float().cpu(), block.cpu())
+        assert (acc, branch) == (racc, rbranch), step
+        np.testing.assert_array_equal(ids.cpu().numpy(), rids)
+        # the reference's commit (generation/d3_generator.py:227-232) of the same rows
+        for l, (k, v) in enumerate(new_kv):
+            lay = ref_cache.layers[l]
+            lay.keys = torch.cat([lay.keys, k[branch:branch + 1, :, :acc]], dim=2)
+            lay.values = torch.cat([lay.values, v[branch:branch + 1, :, :acc]], dim=2)
+        paged.length = L0 + acc
+        for l in range(nl):
+            gk, gv = paged.gather(l)
+            assert torch.equal(gk, ref_cache.layers[l].keys[0].transpose(0, 1)), (step, l)
+            assert torch.equal(gv, ref_cache.layers[l].values[0].transpose(0, 1)), (step, l)
+        anchor = int(ids[-1])

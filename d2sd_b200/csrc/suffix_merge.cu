@@ -8,23 +8,25 @@
 // tokens, then merge_state_in_place into the level-1 state; the sink rescale
 // out *= sigmoid(lse - sink) follows at generation/verification.py:173-176.
 //
-// The work is small and memory-bound (the level-2 attention of a block is at
-// most 64 keys per row; the merge reads each row's partial states), so this is
-// a high-occupancy SIMT kernel: one launch covers every branch; a CTA of 256
-// threads takes RP (32, 16 or 8) consecutive rows of one (block, kv head),
-// rows being token*G + g for the G query heads of the kv head.
-//   phase 1  the block's K/V of the kv head (only the keys the CTA's rows can
-//            see) are staged in shared memory; each warp computes the level-2
-//            attention of 4 rows, its four 8-lane groups splitting the keys:
-//            scores into shared memory, a warp-wide softmax, then P.V with a
-//            reduce-scatter that leaves each group one row; the normalised row
-//            and its base-2 LSE go to shared memory. Each row's level 2 is
-//            computed once.
-//   phase 2  (after the previous kernel -- kernel (a) -- has completed) each
-//            row's lane groups merge the local state with every partial state
-//            kernel (a) wrote for the row's query tile (or with a dense prefix
-//            state), apply the sink factor and store the row once; with the
-//            fused output exchange the row goes to every rank's buffer.
+// One launch covers every branch. Rows are token*G + g (the G query heads of a
+// kv head), cut into 128-row tiles; a tile spans tile_blocks whole blocks when
+// block_len * G divides 128 (so short blocks fill the tile), else it lies in
+// one block. A CTA of 256 threads takes RP rows of one tile (RP = 128 when
+// tiles are plenty; 64 .. 8 when few tiles would leave SMs idle, the level 2 of
+// the tile then being recomputed by each of its CTAs):
+//   phase 1  thread 0 TMA-loads the tile's Q and the keys/values of its blocks
+//            and issues S = Q K^T on tcgen05 into TMEM (M=128, N=32 or 64);
+//            warps 0-3 (thread = row = TMEM lane) mask (same block, and causal,
+//            full or a custom bitmask inside it), exponentiate and write P back
+//            to TMEM; thread 0 issues O = P V (A from TMEM, V MN-major). The
+//            CTA's rows of O, normalised, are staged in bf16 over the Q tile --
+//            the precision in which the reference's level-2 output reaches its
+//            merge -- with their base-2 LSEs.
+//   phase 2  (after the previous kernel -- kernel (a) -- has completed) 8-lane
+//            groups merge each row's local state with every partial state
+//            kernel (a) wrote for its query tile (or a dense prefix state),
+//            apply the sink factor and store the row once (with the fused output
+//            exchange, into every rank's buffer).
 #include "common.cuh"
 #include "plan_layout.h"
 
@@ -36,10 +38,9 @@ namespace {
 using namespace plan;
 
 constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
 constexpr int kGroups = kThreads / 8;  // 8-lane groups of the merge
 constexpr int kMaxBlockLen = 64;
-constexpr int kMaxRows = 32;           // rows of one CTA (4 per warp in phase 1)
+constexpr int kPanelQ = 128 * 128;     // 128 rows x 128 bytes
 
 struct SuffixParams {
   const void* q;
@@ -64,8 +65,9 @@ struct SuffixParams {
   int32_t has_local;
   int32_t block_len, mask_mode, sink_mode;
   int32_t Hq, G;
-  int32_t rows_per_cta;  // RP: 32, 16 or 8
-  int32_t rows_per_unit; // rows of one (block, kv head): block_len * G
+  int32_t rows_per_cta;  // RP: 128, 64, 32, 16 or 8 rows of a 128-row tile
+  int32_t tile_blocks;   // blocks one tile spans (its keys: tile_blocks * block_len)
+  int32_t num_tokens;    // num_blocks * block_len
   float scale_log2;
   // fused output exchange (d2sd_suffix_merge_gather); world == 0: rows go to out
   void* const* peer_out;               // [2][world]: output buffers of each epoch parity
@@ -94,6 +96,7 @@ template <typename T>
 struct Fmt;
 template <>
 struct Fmt<__nv_bfloat16> {
+  static constexpr uint32_t kUmma = 1;  // tcgen05 kind::f16 operand format
   static __device__ __forceinline__ uint32_t pack(float a, float b) { return pack_bf16x2(a, b); }
   // the 8 elements of a 16-byte vector as floats
   static __device__ __forceinline__ void unpack(const uint4& v, float (&f)[8]) {
@@ -107,6 +110,7 @@ struct Fmt<__nv_bfloat16> {
 };
 template <>
 struct Fmt<__half> {
+  static constexpr uint32_t kUmma = 0;
   static __device__ __forceinline__ uint32_t pack(float a, float b) {
     __half2 v = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&v);
@@ -133,74 +137,71 @@ struct RowMeta {
   int32_t pad[2];
 };
 
-// Shared memory of a CTA (bytes from a 16-byte aligned base): the block's K
-// and V rows [keys][D], the scores / probabilities of phase 1 [warp][key][4
-// rows], the normalised local outputs [RP][D + 4] fp32 and the row metadata.
-struct SmemLayout {
-  int k, v, p, stage, meta, total;
-  __host__ __device__ SmemLayout(int keys, int D, int elem) {
-    k = 0;
-    v = k + keys * D * elem;
-    p = v + keys * D * elem;
-    stage = p + kWarps * kMaxBlockLen * 16;
-    meta = stage + kMaxRows * (D + 4) * 4;
-    total = meta + kMaxRows * static_cast<int>(sizeof(RowMeta));
-  }
+template <int D, int NK>
+struct SCfg {
+  static constexpr int kPanels = D / 64;
+  static constexpr int kPanelKV = NK * 128;
+  static constexpr int kQBytes = 128 * D * 2;
+  static constexpr int kKVBytes = NK * D * 2;
+  static constexpr int kSmemQ = 0;
+  static constexpr int kSmemK = kQBytes;
+  static constexpr int kSmemV = kSmemK + kKVBytes;
+  static constexpr int kSmemBar = kSmemV + kKVBytes;
+  static constexpr int kSmemMeta = kSmemBar + 64;
+  static constexpr int kSmemBytes = kSmemMeta + kTileRows * 32 + 1024;  // + align slack
+  static constexpr int kStageRow = D + 8;  // bf16 row of the staged local output
+  // the staged local output [128][D + 8] bf16 reuses the Q/K/V region
+  static_assert(kTileRows * kStageRow * 2 <= kSmemBar, "stage does not fit");
 };
 
-__device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int o) {
-  return __shfl_xor_sync(0xffffffffu, static_cast<unsigned long long>(v), o);
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) {
+    while (!mbar_try_wait(bar, parity)) {
+    }
+  }
+  return ok != 0;
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 2) suffix_merge_kernel(const SuffixParams p) {
-  constexpr int NC = D / 64;  // 64-column chunks of a row
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int TB = p.block_len, G = p.G, RP = p.rows_per_cta;
-  const int blk = blockIdx.x, h = blockIdx.y, r0 = blockIdx.z * RP;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const SmemLayout sl(p.has_local ? TB : 0, D, static_cast<int>(sizeof(T)));
-  float4* pbuf = reinterpret_cast<float4*>(smem + sl.p);
-  float* stage = reinterpret_cast<float*>(smem + sl.stage);
-  RowMeta* meta = reinterpret_cast<RowMeta*>(smem + sl.meta);
-  constexpr int SP = D + 4;  // padded fp32 row of the staged local output
+template <typename T, int D, int NK>
+__global__ void __launch_bounds__(kThreads, 2)
+    suffix_merge_kernel(const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const SuffixParams p) {
+  using C = SCfg<D, NK>;
+  constexpr int SP = C::kStageRow;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kSmemBar);  // load, S, O
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  RowMeta* meta = reinterpret_cast<RowMeta*>(smem + C::kSmemMeta);
+  T* stage = reinterpret_cast<T*>(smem + C::kSmemQ);  // reuses Q/K/V after the MMAs
+
+  const int gx = blockIdx.x, h = blockIdx.y;
+  // 128-row tile rt of token group gx, CTA part `part` = rows [part*RP, part*RP + RP)
+  const int RP = p.rows_per_cta;
+  const int parts = kTileRows / RP;
+  const int rt = blockIdx.z / parts, part = blockIdx.z - (blockIdx.z / parts) * parts;
+  const int TB = p.block_len, G = p.G;
+  const int KB = p.tile_blocks * TB;  // tokens of the group (its keys)
+  const int gt0 = gx * KB;            // first token of the group
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const float sl2 = p.scale_log2;
   // the next kernel may set itself up now; it waits for this one to complete
   grid_dep_launch();
 
-  // keys the CTA's rows can see: a causal row of token t sees keys 0..t
-  const int t_last = min(TB - 1, (r0 + RP - 1) / G);
-  const int nkeys =
-      !p.has_local ? 0 : (p.mask_mode == D2SD_MASK_CAUSAL ? t_last + 1 : TB);
-
-  // ---- the block's K/V rows of this kv head into shared memory (loads first,
-  // then the row metadata while they are in flight, then the stores) ----
-  constexpr int VR = D * static_cast<int>(sizeof(T)) / 16;  // 16-byte vectors per row
-  constexpr int EV = 16 / static_cast<int>(sizeof(T));      // elements per vector
-  const int nvec = nkeys * VR;
-  uint4 kvbuf[4];
-  int kvdst[4];
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int i = threadIdx.x + u * kThreads;
-    kvdst[u] = -1;
-    if (i < 2 * nvec) {
-      const int kv = i >= nvec;
-      const int ii = kv ? i - nvec : i;
-      const int j = ii / VR, c = ii - (ii / VR) * VR;
-      const T* src = static_cast<const T*>(kv ? p.v_local : p.k_local) +
-                     static_cast<int64_t>(blk * TB + j) * p.kv_st +
-                     static_cast<int64_t>(h) * p.kv_sh + c * EV;
-      kvbuf[u] = *reinterpret_cast<const uint4*>(src);
-      kvdst[u] = (kv ? sl.v : sl.k) + ii * 16;
-    }
-  }
-  if (threadIdx.x < RP) {
-    // row metadata from the (static) plan: the partial slots of the row's query tile
-    const int lr = threadIdx.x;
-    const int Rm = r0 + lr;
+  // ---- row metadata of this CTA's rows from the (static) plan: warps 4-7,
+  // idle during the level-2 attention, so the lookups overlap it ----
+  if (threadIdx.x >= 128 && threadIdx.x - 128 < RP) {
+    const int lr = threadIdx.x - 128;
+    const int Rm = rt * kTileRows + part * RP + lr;
     const int tm = Rm / G, gm = Rm - (Rm / G) * G;
-    const bool vm = tm < TB;
-    const int tokm = blk * TB + tm;
+    const bool vm = tm < KB && gt0 + tm < p.num_tokens;
+    const int tokm = gt0 + tm;
     int slot = 0, nslots = 0, prow = 0;
     if (vm && p.partial) {
       const int32_t* pl = p.plan;
@@ -216,190 +217,165 @@ __global__ void __launch_bounds__(kThreads, 2) suffix_merge_kernel(const SuffixP
         prow = qrow % kTileRows;
       }
     }
-    meta[lr].lse_local = -INFINITY;
+    // lse_local is written by the warps that own the row's TMEM lane
     meta[lr].tok = vm ? tokm : -1;
     meta[lr].hq = h * G + gm;
     meta[lr].slot = slot;
     meta[lr].nslots = nslots;
     meta[lr].prow = prow;
   }
-#pragma unroll
-  for (int u = 0; u < 4; ++u)
-    if (kvdst[u] >= 0) *reinterpret_cast<uint4*>(smem + kvdst[u]) = kvbuf[u];
-  for (int i = threadIdx.x + 4 * kThreads; i < 2 * nvec; i += kThreads) {  // block_len > 32 at D 128
-    const int kv = i >= nvec;
-    const int ii = kv ? i - nvec : i;
-    const int j = ii / VR, c = ii - (ii / VR) * VR;
-    const T* src = static_cast<const T*>(kv ? p.v_local : p.k_local) +
-                   static_cast<int64_t>(blk * TB + j) * p.kv_st + static_cast<int64_t>(h) * p.kv_sh +
-                   c * EV;
-    *reinterpret_cast<uint4*>(smem + (kv ? sl.v : sl.k) + ii * 16) =
-        *reinterpret_cast<const uint4*>(src);
-  }
-  __syncthreads();
 
-  // ---- phase 1: level-2 attention, 4 rows per warp. Lane j8 of 8-lane group
-  // gi holds columns {c*64 + 8*j8 + e}; for the scores and P.V the groups split
-  // the keys (group gi takes keys gi, gi+4, ...) ----
-  if (p.has_local && warp * 4 < RP) {
-    const int gi = lane >> 3, j8 = lane & 7;
-    const float sl2 = p.scale_log2;
-    uint64_t allowed[4];
-    uint64_t qf[4][NC * 4];  // the rows' q at this lane's columns, fp32 pairs
+  // ---- phase 1: level-2 attention of the tile on tcgen05 (warps 0-3, thread = row) ----
+  uint32_t tmem = 0;
+  bool ok = true;
+  float lse_l = -INFINITY, inv_l = 0.f;
+  const int row = threadIdx.x & 127;  // TMEM lane of warps 0-3
+  const int tr = (rt * kTileRows + row) / G;  // token of the row inside the group
+  if (p.has_local) {
+    if (threadIdx.x == 0) {
+      for (int b = 0; b < 3; ++b) mbar_init(&bars[b], 1);
+      *abort = 0;
+      fence_mbar_init();
+      fence_proxy_async_smem();
+    }
+    if (warp == 0) {
+      tmem_alloc(tmem_slot, 256);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    tmem = *tmem_slot;
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&bars[0], C::kQBytes + 2 * C::kKVBytes);
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int R = r0 + 4 * warp + r;
-      const int t = R / G, g = R - (R / G) * G;
-      const bool valid = t < TB;
-      const int tok = blk * TB + t;
-      uint64_t m = 0;
-      if (valid) {
-        if (p.mask_mode == D2SD_MASK_CAUSAL) m = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
-        else if (p.mask_mode == D2SD_MASK_CUSTOM) m = p.custom_mask[tok];
-        else m = ~0ull;
-        if (TB < 64) m &= (1ull << TB) - 1ull;
+      for (int pn = 0; pn < C::kPanels; ++pn) {
+        tma_load_3d(smem + C::kSmemQ + pn * kPanelQ, &tm_q, &bars[0], pn * 64, h * G,
+                    gt0 + rt * (kTileRows / G));
+        tma_load_3d(smem + C::kSmemK + pn * C::kPanelKV, &tm_k, &bars[0], pn * 64, h, gt0);
+        tma_load_3d(smem + C::kSmemV + pn * C::kPanelKV, &tm_v, &bars[0], pn * 64, h, gt0);
       }
-      allowed[r] = m;
+      if (mbar_wait(&bars[0], 0, abort)) {
+        tc_fence_after();
+        constexpr uint32_t idesc = umma_idesc(128, NK, false, Fmt<T>::kUmma);
+        const uint32_t a0 = smem_u32(smem + C::kSmemQ);
+        const uint32_t b0 = smem_u32(smem + C::kSmemK);
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-        if (valid)
-          raw = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
-                                                static_cast<int64_t>(tok) * p.q_st +
-                                                static_cast<int64_t>(h * G + g) * p.q_sh +
-                                                c * 64 + 8 * j8);
-        float f[8];
-        Fmt<T>::unpack(raw, f);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) qf[r][c * 4 + k] = f2_pack(f[2 * k], f[2 * k + 1]);
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint32_t ka = (ks / 4) * kPanelQ + (ks % 4) * 32;
+          const uint32_t kb = (ks / 4) * C::kPanelKV + (ks % 4) * 32;
+          umma_ss(tmem, umma_desc_sw128(a0 + ka, 16, 1024), umma_desc_sw128(b0 + kb, 16, 1024),
+                  idesc, ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&bars[1]);
       }
     }
-    float4* pw = pbuf + warp * kMaxBlockLen;  // [key] -> the 4 rows' scores, then probabilities
-    const int iters = (nkeys + 3) / 4;
-    for (int it = 0; it < iters; ++it) {
-      const int j = gi + 4 * it;
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      if (j < nkeys) {
-        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+    if (warp < 4) {
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      ok = warp_wait(&bars[1], 0, abort);
+      if (ok) {
+        tc_fence_after();
+        uint32_t s[NK];
+        tmem_ld32_wait(lane_base, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+        if (NK == 64)
+          tmem_ld32_wait(lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32 % NK]));
+        // keys of the group are its tokens 0..KB-1: the row sees only its own
+        // block's keys, and inside the block the causal / custom / full mask
+        uint64_t allowed = 0;
+        if (tr < KB && gt0 + tr < p.num_tokens) {
+          const int b = tr / TB, pos = tr - (tr / TB) * TB;
+          uint64_t w;
+          if (p.mask_mode == D2SD_MASK_CAUSAL) w = (pos >= 63) ? ~0ull : ((2ull << pos) - 1ull);
+          else if (p.mask_mode == D2SD_MASK_CUSTOM) w = p.custom_mask[gt0 + tr];
+          else w = ~0ull;
+          if (TB < 64) w &= (1ull << TB) - 1ull;
+          allowed = w << (b * TB);  // b * TB < KB <= 64
+        }
+        float m = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          const uint4 kk = *reinterpret_cast<const uint4*>(
-              smem + sl.k + (static_cast<int>(j) * D + c * 64 + 8 * j8) * static_cast<int>(sizeof(T)));
-          float kf[8];
-          Fmt<T>::unpack(kk, kf);
+        for (int j = 0; j < NK; ++j) {
+          if (!((allowed >> j) & 1ull)) s[j] = 0xff800000u;
+          m = fmaxf(m, __uint_as_float(s[j]));
+        }
+        const float mm = (m == -INFINITY) ? 0.f : m * sl2;
+        float l = 0.f;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t k2 = f2_pack(kf[2 * k], kf[2 * k + 1]);
+        for (int c = 0; c < NK / 32; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) acc[r] = f2_fma(qf[r][c * 4 + k], k2, acc[r]);
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e]), sl2, -mm));
+            const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, -mm));
+            l += p0 + p1;
+            pk[e] = Fmt<T>::pack(p0, p1);
           }
+          tmem_st16(lane_base + c * 16, pk);
         }
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          float x, y;
-          f2_unpack(acc[r], x, y);
-          d[r] = x + y;
+        tmem_st_wait();
+        if (l > 0.f) {
+          lse_l = mm + fast_log2(l);
+          inv_l = 1.f / l;
         }
-      }
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) d[r] += __shfl_xor_sync(0xffffffffu, d[r], o);
-      if (j8 == 0 && j < nkeys) {
-        float4 s;
-        s.x = ((allowed[0] >> j) & 1ull) ? d[0] * sl2 : -INFINITY;
-        s.y = ((allowed[1] >> j) & 1ull) ? d[1] * sl2 : -INFINITY;
-        s.z = ((allowed[2] >> j) & 1ull) ? d[2] * sl2 : -INFINITY;
-        s.w = ((allowed[3] >> j) & 1ull) ? d[3] * sl2 : -INFINITY;
-        pw[j] = s;
       }
     }
-    __syncwarp();
-    // softmax of the 4 rows over the keys: lane L holds keys L and L + 32
-    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    float4 sa = lane < nkeys ? pw[lane] : ninf;
-    float4 sb = lane + 32 < nkeys ? pw[lane + 32] : ninf;
-    float m[4] = {fmaxf(sa.x, sb.x), fmaxf(sa.y, sb.y), fmaxf(sa.z, sb.z), fmaxf(sa.w, sb.w)};
+    tc_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0 && !*abort) {
+      tc_fence_after();
+      constexpr uint32_t idesc = umma_idesc(128, D, true, Fmt<T>::kUmma);
+      const uint32_t b0 = smem_u32(smem + C::kSmemV);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], o));
-#pragma unroll
-    for (int r = 0; r < 4; ++r) m[r] = (m[r] == -INFINITY) ? 0.f : m[r];
-    sa = make_float4(fast_exp2(sa.x - m[0]), fast_exp2(sa.y - m[1]), fast_exp2(sa.z - m[2]),
-                     fast_exp2(sa.w - m[3]));
-    sb = make_float4(fast_exp2(sb.x - m[0]), fast_exp2(sb.y - m[1]), fast_exp2(sb.z - m[2]),
-                     fast_exp2(sb.w - m[3]));
-    float l[4] = {sa.x + sb.x, sa.y + sb.y, sa.z + sb.z, sa.w + sb.w};
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int r = 0; r < 4; ++r) l[r] += __shfl_xor_sync(0xffffffffu, l[r], o);
-    if (lane < nkeys) pw[lane] = sa;
-    if (lane + 32 < nkeys) pw[lane + 32] = sb;
-    __syncwarp();
-    // this group's row (gi) after the reduce-scatter below
-    const float l_g = gi == 0 ? l[0] : gi == 1 ? l[1] : gi == 2 ? l[2] : l[3];
-    const float m_g = gi == 0 ? m[0] : gi == 1 ? m[1] : gi == 2 ? m[2] : m[3];
-    const float inv_g = l_g > 0.f ? 1.f / l_g : 0.f;
-    const int lr_g = 4 * warp + gi;
-    // P.V, 64 columns at a time
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-      uint64_t o[4][4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) o[r][k] = 0ull;
-      for (int it = 0; it < iters; ++it) {
-        const int j = gi + 4 * it;
-        if (j >= nkeys) break;
-        const float4 pj = pw[j];
-        const uint4 vv = *reinterpret_cast<const uint4*>(
-            smem + sl.v + (j * D + c * 64 + 8 * j8) * static_cast<int>(sizeof(T)));
-        float vf[8];
-        Fmt<T>::unpack(vv, vf);
-        const uint64_t p2[4] = {f2_pack(pj.x, pj.x), f2_pack(pj.y, pj.y), f2_pack(pj.z, pj.z),
-                                f2_pack(pj.w, pj.w)};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t v2 = f2_pack(vf[2 * k], vf[2 * k + 1]);
-#pragma unroll
-          for (int r = 0; r < 4; ++r) o[r][k] = f2_fma(p2[r], v2, o[r][k]);
-        }
+      for (int ks = 0; ks < NK / 16; ++ks) {
+        umma_ts(tmem + 128, tmem + ks * 8, umma_desc_sw128(b0 + ks * 16 * 128, C::kPanelKV, 1024),
+                idesc, ks > 0 ? 1u : 0u);
       }
-      // reduce-scatter over the four groups: group gi ends with row gi
-      const bool hi = (gi & 2) != 0, lo = (gi & 1) != 0;
-      uint64_t res[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint64_t keep0 = hi ? o[2][k] : o[0][k], send0 = hi ? o[0][k] : o[2][k];
-        uint64_t keep1 = hi ? o[3][k] : o[1][k], send1 = hi ? o[1][k] : o[3][k];
-        keep0 = f2_add(keep0, shfl_xor_u64(send0, 16));
-        keep1 = f2_add(keep1, shfl_xor_u64(send1, 16));
-        const uint64_t keep = lo ? keep1 : keep0, send = lo ? keep0 : keep1;
-        res[k] = f2_add(keep, shfl_xor_u64(send, 8));
-      }
-      if (lr_g < RP) {
-        float* dst = stage + lr_g * SP + c * 64 + 8 * j8;
-        float a0, a1, b0, b1, c0, c1, d0, d1;
-        f2_unpack(res[0], a0, a1);
-        f2_unpack(res[1], b0, b1);
-        f2_unpack(res[2], c0, c1);
-        f2_unpack(res[3], d0, d1);
-        reinterpret_cast<float4*>(dst)[0] = make_float4(a0 * inv_g, a1 * inv_g, b0 * inv_g, b1 * inv_g);
-        reinterpret_cast<float4*>(dst)[1] = make_float4(c0 * inv_g, c1 * inv_g, d0 * inv_g, d1 * inv_g);
-      }
+      umma_commit(&bars[2]);
     }
-    if (j8 == 0 && lr_g < RP) meta[lr_g].lse_local = l_g > 0.f ? m_g + fast_log2(l_g) : -INFINITY;
+    if (warp < 4) {
+      ok = warp_wait(&bars[2], 0, abort) && ok;
+      tc_fence_after();
+    }
   }
-  __syncthreads();
 
-  // ---- phase 2: merge. The CTA's 32 lane groups of 8 lanes (4 per warp) are
-  // spread over its RP rows, GS = 32 / RP groups per row (in the same warp); a
-  // group takes every GS-th slot of its row, 8 lanes across the row's columns
-  // (D/8 each), with up to 8 slot rows and all their LSEs in flight before any
-  // use; the row's groups then add their partial sums with shuffles.
+  // ---- phase 1b: this CTA's rows of the local O, normalised, into the bf16
+  // stage over the Q/K/V tiles (free once both MMAs completed). Warp w (< 4)
+  // owns TMEM lanes [32w, 32w + 32); it takes part if they meet the CTA's rows ----
+  if (warp < 4 && warp * 32 < RP * (part + 1) && warp * 32 + 32 > RP * part) {
+    const int lr = row - RP * part;
+    const bool mine = lr >= 0 && lr < RP;
+    if (mine) meta[lr].lse_local = (p.has_local && ok) ? lse_l : -INFINITY;
+    if (p.has_local) {
+      const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      const float sc = ok ? inv_l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32_wait(lane_base + 128 + c * 32, o);
+        if (!mine) continue;
+        uint4* dst = reinterpret_cast<uint4*>(stage + lr * SP + c * 32);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          dst[e] = make_uint4(Fmt<T>::pack(__uint_as_float(o[8 * e]) * sc, __uint_as_float(o[8 * e + 1]) * sc),
+                              Fmt<T>::pack(__uint_as_float(o[8 * e + 2]) * sc, __uint_as_float(o[8 * e + 3]) * sc),
+                              Fmt<T>::pack(__uint_as_float(o[8 * e + 4]) * sc, __uint_as_float(o[8 * e + 5]) * sc),
+                              Fmt<T>::pack(__uint_as_float(o[8 * e + 6]) * sc, __uint_as_float(o[8 * e + 7]) * sc));
+      }
+    }
+  }
+  if (p.has_local) tc_fence_before();
+  __syncthreads();
+  if (p.has_local && warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+  if (p.has_local && threadIdx.x == 0 && *abort && p.status) atomicExch(p.status, 2);
+
+  // ---- phase 2: merge. The CTA's 32 lane groups of 8 lanes (4 per warp)
+  // take its RP rows in passes of 32 rows (GS = 1 group per row), or, with
+  // fewer rows, GS = 32 / RP groups per row (in the same warp); a group takes
+  // every GS-th slot of its row, 8 lanes across the row's columns (D/8 each),
+  // with up to 8 slot rows and all their LSEs in flight before any use; the
+  // row's groups then add their partial sums with shuffles.
   // The partial slots come from the previous kernel (kernel (a)): wait for it.
   // Phase 1 read only q and the block's K/V, which precede kernel (a).
   grid_dep_wait();
@@ -407,20 +383,12 @@ __global__ void __launch_bounds__(kThreads, 2) suffix_merge_kernel(const SuffixP
   constexpr int VEC = CPL * 2 / 16;   // 16-byte vectors per lane and slot row
   constexpr int kBatch = 8;           // slot rows in flight per lane
   constexpr int kLseBlocks = 4;       // LSE blocks of 8 slots loaded together
-  const int GS = kGroups / RP;        // lane groups per row: 1, 2 or 4
+  const int GS = RP >= kGroups ? 1 : kGroups / RP;  // lane groups per row: 1, 2 or 4
+  const int passes = RP >= kGroups ? RP / kGroups : 1;
   const int64_t sbytes = slot_bytes(D);
   const uint8_t* part_base = static_cast<const uint8_t*>(p.partial);
   const int gi = warp * 4 + (lane >> 3), j8 = lane & 7;
-  const int lr = gi / GS, sg = gi - (gi / GS) * GS;  // row, slot group of the row
-  const RowMeta mt = meta[lr];
-  const bool live = mt.tok >= 0;
-  const int nslots = live ? mt.nslots : 0;
-  // the group's slots: sg, sg + GS, ...; k-th of them
-  const int nmine = nslots > sg ? (nslots - sg + GS - 1) / GS : 0;
-  // loops that shuffle run the warp's largest count (rows of a warp may map to
-  // different query tiles, e.g. with a shared trunk); lanes past their own
-  // count are predicated off
-  const int nmine_w = __reduce_max_sync(0xffffffffu, nmine);
+  const int sg = gi - (gi / GS) * GS;  // slot group of the row
   auto gmax = [GS](float v) {  // max over the row's lanes
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -438,136 +406,148 @@ __global__ void __launch_bounds__(kThreads, 2) suffix_merge_kernel(const SuffixP
     if (GS > 2) v += __shfl_xor_sync(0xffffffffu, v, 16);
     return v;
   };
-  const uint8_t* prow_base =
-      part_base ? part_base + static_cast<int64_t>(mt.prow) * D * 2 + j8 * CPL * 2 : nullptr;
-  auto slot_of = [&](int k) { return mt.slot + sg + GS * k; };
-  auto slot_lse = [&](int k) -> float {
-    return *reinterpret_cast<const float*>(part_base + slot_of(k) * sbytes + kTileRows * D * 2 +
-                                           mt.prow * 4);
-  };
-  auto load_batch = [&](int k0, uint4 (&r)[kBatch][VEC]) {
+#pragma unroll 1
+  for (int ps = 0; ps < passes; ++ps) {
+    const int lr = GS == 1 ? ps * kGroups + gi : gi / GS;
+    const RowMeta mt = meta[lr];
+    const bool live = mt.tok >= 0;
+    const int nslots = live ? mt.nslots : 0;
+    // the group's slots: sg, sg + GS, ...; k-th of them
+    const int nmine = nslots > sg ? (nslots - sg + GS - 1) / GS : 0;
+    // loops that shuffle run the warp's largest count (rows of a warp may map
+    // to different query tiles); lanes past their own count are predicated off
+    const int nmine_w = __reduce_max_sync(0xffffffffu, nmine);
+    const uint8_t* prow_base =
+        part_base ? part_base + static_cast<int64_t>(mt.prow) * D * 2 + j8 * CPL * 2 : nullptr;
+    auto slot_of = [&](int k) { return mt.slot + sg + GS * k; };
+    auto slot_lse = [&](int k) -> float {
+      return *reinterpret_cast<const float*>(part_base + slot_of(k) * sbytes + kTileRows * D * 2 +
+                                             mt.prow * 4);
+    };
+    auto load_batch = [&](int k0, uint4 (&r)[kBatch][VEC]) {
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      if (k0 + j < nmine) {
+      for (int j = 0; j < kBatch; ++j) {
+        if (k0 + j < nmine) {
 #pragma unroll
-        for (int c = 0; c < VEC; ++c)
-          r[j][c] = reinterpret_cast<const uint4*>(prow_base + slot_of(k0 + j) * sbytes)[c];
+          for (int c = 0; c < VEC; ++c)
+            r[j][c] = reinterpret_cast<const uint4*>(prow_base + slot_of(k0 + j) * sbytes)[c];
+        }
+      }
+    };
+    // first batch of slot rows and the LSEs of up to 8 * kLseBlocks slots of
+    // the group (lane j8 holds the LSE of the group's slot j8 + 8b), all in flight
+    uint4 v[kBatch][VEC];
+    load_batch(0, v);
+    float ls[kLseBlocks];
+#pragma unroll
+    for (int b = 0; b < kLseBlocks; ++b) ls[b] = (8 * b + j8 < nmine) ? slot_lse(8 * b + j8) : -INFINITY;
+    // dense prefix state (no partial slots)
+    float lse_p = -INFINITY;
+    const T* po = nullptr;
+    if (live && !p.partial && p.prefix_out) {
+      po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(mt.tok) * p.po_st +
+           static_cast<int64_t>(mt.hq) * p.po_sh + j8 * CPL;
+      lse_p = p.prefix_lse[static_cast<int64_t>(mt.tok) * p.pl_st + mt.hq];
+    }
+    const float lse_local = live ? mt.lse_local : -INFINITY;
+    float lmax = -INFINITY;
+#pragma unroll
+    for (int b = 0; b < kLseBlocks; ++b) lmax = fmaxf(lmax, ls[b]);
+    for (int k0 = 8 * kLseBlocks; k0 < nmine_w; k0 += 8)  // very many slots
+      lmax = fmaxf(lmax, k0 + j8 < nmine ? slot_lse(k0 + j8) : -INFINITY);
+    const float M = fmaxf(fmaxf(lse_local, lse_p), gmax(lmax));
+    const float Mz = (M == -INFINITY) ? 0.f : M;
+    const float w_l = (lse_local == -INFINITY) ? 0.f : fast_exp2(lse_local - Mz);
+    const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
+    float acc[CPL];
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
+    if (sg == 0) {  // the local and dense-prefix states enter once per row
+      if (p.has_local && live) {
+        const uint4* st = reinterpret_cast<const uint4*>(stage + lr * SP + j8 * CPL);
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) {
+          float f[8];
+          Fmt<T>::unpack(st[c], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[c * 8 + e] = w_l * f[e];
+        }
+      }
+      if (po) {
+#pragma unroll
+        for (int e = 0; e < CPL; ++e) acc[e] = fmaf(w_p, Num<T>::to_f(po[e]), acc[e]);
       }
     }
-  };
-  // first batch of slot rows and the LSEs of up to 8 * kLseBlocks slots of the
-  // group (lane j8 holds the LSE of the group's slot j8 + 8b), all in flight
-  uint4 v[kBatch][VEC];
-  load_batch(0, v);
-  float ls[kLseBlocks];
+    auto add_row = [&](float wj, const uint4 (&r)[VEC]) {
 #pragma unroll
-  for (int b = 0; b < kLseBlocks; ++b) ls[b] = (8 * b + j8 < nmine) ? slot_lse(8 * b + j8) : -INFINITY;
-  // dense prefix state (no partial slots)
-  float lse_p = -INFINITY;
-  const T* po = nullptr;
-  if (live && !p.partial && p.prefix_out) {
-    po = static_cast<const T*>(p.prefix_out) + static_cast<int64_t>(mt.tok) * p.po_st +
-         static_cast<int64_t>(mt.hq) * p.po_sh + j8 * CPL;
-    lse_p = p.prefix_lse[static_cast<int64_t>(mt.tok) * p.pl_st + mt.hq];
-  }
-  const float lse_local = live ? mt.lse_local : -INFINITY;
-  float lmax = -INFINITY;
+      for (int c = 0; c < VEC; ++c) {
+        const uint32_t u[4] = {r[c].x, r[c].y, r[c].z, r[c].w};
 #pragma unroll
-  for (int b = 0; b < kLseBlocks; ++b) lmax = fmaxf(lmax, ls[b]);
-  for (int k0 = 8 * kLseBlocks; k0 < nmine_w; k0 += 8)  // very many slots
-    lmax = fmaxf(lmax, k0 + j8 < nmine ? slot_lse(k0 + j8) : -INFINITY);
-  const float M = fmaxf(fmaxf(lse_local, lse_p), gmax(lmax));
-  const float Mz = (M == -INFINITY) ? 0.f : M;
-  const float w_l = (lse_local == -INFINITY) ? 0.f : fast_exp2(lse_local - Mz);
-  const float w_p = (lse_p == -INFINITY) ? 0.f : fast_exp2(lse_p - Mz);
-  float acc[CPL];
+        for (int k = 0; k < 4; ++k) {
+          acc[c * 8 + 2 * k] = fmaf(wj, __uint_as_float(u[k] << 16), acc[c * 8 + 2 * k]);
+          acc[c * 8 + 2 * k + 1] =
+              fmaf(wj, __uint_as_float(u[k] & 0xffff0000u), acc[c * 8 + 2 * k + 1]);
+        }
+      }
+    };
+    float den = 0.f;
+    for (int k0 = 0; k0 < nmine_w; k0 += kBatch) {
+      if (k0 > 0) load_batch(k0, v);  // later batches: 8 rows in flight again
+      const int b = k0 / 8;
+      float l = -INFINITY;
+      if (b < kLseBlocks) {
 #pragma unroll
-  for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
-  if (sg == 0) {  // the local and dense-prefix states enter once per row
-    if (p.has_local && live) {
-      const float4* st = reinterpret_cast<const float4*>(stage + lr * SP + j8 * CPL);
+        for (int q = 0; q < kLseBlocks; ++q)
+          if (q == b) l = ls[q];
+      } else if (k0 + j8 < nmine) {
+        l = slot_lse(k0 + j8);
+      }
+      const float w = (l == -INFINITY) ? 0.f : fast_exp2(l - Mz);  // weight of slot k0 + j8
+      den += gsum8(w);
 #pragma unroll
-      for (int e = 0; e < CPL / 4; ++e) {
-        const float4 x = st[e];
-        acc[4 * e] = w_l * x.x;
-        acc[4 * e + 1] = w_l * x.y;
-        acc[4 * e + 2] = w_l * x.z;
-        acc[4 * e + 3] = w_l * x.w;
+      for (int j = 0; j < kBatch; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, (lane & ~7) + j);
+        if (k0 + j < nmine) add_row(wj, v[j]);
       }
     }
-    if (po) {
+    // the row's groups add up: acc, den over groups (the local/prefix weights once)
 #pragma unroll
-      for (int e = 0; e < CPL; ++e) acc[e] = fmaf(w_p, Num<T>::to_f(po[e]), acc[e]);
-    }
-  }
-  auto add_row = [&](float wj, const uint4 (&r)[VEC]) {
-#pragma unroll
-    for (int c = 0; c < VEC; ++c) {
-      const uint32_t u[4] = {r[c].x, r[c].y, r[c].z, r[c].w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        acc[c * 8 + 2 * k] = fmaf(wj, __uint_as_float(u[k] << 16), acc[c * 8 + 2 * k]);
-        acc[c * 8 + 2 * k + 1] = fmaf(wj, __uint_as_float(u[k] & 0xffff0000u), acc[c * 8 + 2 * k + 1]);
+    for (int e = 0; e < CPL; ++e) acc[e] = rsum(acc[e]);
+    den = rsum(den) + w_l + w_p;
+    if (live && sg == 0) {
+      const float lse_out = den > 0.f ? Mz + fast_log2(den) : -INFINITY;
+      float factor = den > 0.f ? 1.f / den : 0.f;
+      if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
+        const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse_out * kLn2 : lse_out) - p.sinks[mt.hq];
+        factor *= 1.f / (1.f + __expf(-x));
       }
-    }
-  };
-  float den = 0.f;
-  for (int k0 = 0; k0 < nmine_w; k0 += kBatch) {
-    if (k0 > 0) load_batch(k0, v);  // later batches: 8 rows in flight again
-    const int b = k0 / 8;
-    float l = -INFINITY;
-    if (b < kLseBlocks) {
+      uint4 o[VEC];
 #pragma unroll
-      for (int q = 0; q < kLseBlocks; ++q)
-        if (q == b) l = ls[q];
-    } else if (k0 + j8 < nmine) {
-      l = slot_lse(k0 + j8);
-    }
-    const float w = (l == -INFINITY) ? 0.f : fast_exp2(l - Mz);  // weight of slot k0 + j8
-    den += gsum8(w);
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const float wj = __shfl_sync(0xffffffffu, w, (lane & ~7) + j);
-      if (k0 + j < nmine) add_row(wj, v[j]);
-    }
-  }
-  // the row's groups add up: acc, den over groups (the local/prefix weights once)
-#pragma unroll
-  for (int e = 0; e < CPL; ++e) acc[e] = rsum(acc[e]);
-  den = rsum(den) + w_l + w_p;
-  if (live && sg == 0) {
-    const float lse_out = den > 0.f ? Mz + fast_log2(den) : -INFINITY;
-    float factor = den > 0.f ? 1.f / den : 0.f;
-    if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
-      const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse_out * kLn2 : lse_out) - p.sinks[mt.hq];
-      factor *= 1.f / (1.f + __expf(-x));
-    }
-    uint4 o[VEC];
-#pragma unroll
-    for (int c = 0; c < VEC; ++c) {
-      o[c].x = Fmt<T>::pack(acc[c * 8 + 0] * factor, acc[c * 8 + 1] * factor);
-      o[c].y = Fmt<T>::pack(acc[c * 8 + 2] * factor, acc[c * 8 + 3] * factor);
-      o[c].z = Fmt<T>::pack(acc[c * 8 + 4] * factor, acc[c * 8 + 5] * factor);
-      o[c].w = Fmt<T>::pack(acc[c * 8 + 6] * factor, acc[c * 8 + 7] * factor);
-    }
-    if (p.world == 0) {
-      T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(mt.tok) * p.o_st +
-                static_cast<int64_t>(mt.hq) * p.o_sh + j8 * CPL;
-#pragma unroll
-      for (int c = 0; c < VEC; ++c) reinterpret_cast<uint4*>(orow)[c] = o[c];
-    } else {
-      // the row into every rank's output buffer of this epoch's parity, at this
-      // rank's head offset (NVLink stores for the peers)
-      const int64_t off = static_cast<int64_t>(mt.tok) * p.pg_st +
-                          static_cast<int64_t>(p.head_offset + mt.hq) * p.pg_sh + j8 * CPL;
-      void* const* outs = p.peer_out + (p.epoch & 1) * p.world;
-      for (int d = 0; d < p.world; ++d) {
-        T* orow = static_cast<T*>(outs[d]) + off;
+      for (int c = 0; c < VEC; ++c) {
+        o[c].x = Fmt<T>::pack(acc[c * 8 + 0] * factor, acc[c * 8 + 1] * factor);
+        o[c].y = Fmt<T>::pack(acc[c * 8 + 2] * factor, acc[c * 8 + 3] * factor);
+        o[c].z = Fmt<T>::pack(acc[c * 8 + 4] * factor, acc[c * 8 + 5] * factor);
+        o[c].w = Fmt<T>::pack(acc[c * 8 + 6] * factor, acc[c * 8 + 7] * factor);
+      }
+      if (p.world == 0) {
+        T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(mt.tok) * p.o_st +
+                  static_cast<int64_t>(mt.hq) * p.o_sh + j8 * CPL;
 #pragma unroll
         for (int c = 0; c < VEC; ++c) reinterpret_cast<uint4*>(orow)[c] = o[c];
+      } else {
+        // the row into every rank's output buffer of this epoch's parity, at
+        // this rank's head offset (NVLink stores for the peers)
+        const int64_t off = static_cast<int64_t>(mt.tok) * p.pg_st +
+                            static_cast<int64_t>(p.head_offset + mt.hq) * p.pg_sh + j8 * CPL;
+        void* const* outs = p.peer_out + (p.epoch & 1) * p.world;
+        for (int d = 0; d < p.world; ++d) {
+          T* orow = static_cast<T*>(outs[d]) + off;
+#pragma unroll
+          for (int c = 0; c < VEC; ++c) reinterpret_cast<uint4*>(orow)[c] = o[c];
+        }
       }
+      if (j8 == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
     }
-    if (j8 == 0 && p.lse) p.lse[static_cast<int64_t>(mt.tok) * p.l_st + mt.hq] = lse_out;
   }
 
   if (p.world > 0) {
@@ -656,31 +636,45 @@ __global__ void merge_state_kernel(T* v, int64_t v_st, int64_t v_sh, float* s, i
 
 namespace d2sd {
 namespace {
-// Rows per CTA (32, 16 or 8): fewer, and more lane groups per row, when few
-// rows would leave most SMs idle (KV-head sharding over several GPUs leaves
-// each rank few heads, and each query tile then has many partial slots).
-int rows_per_cta(int64_t rows) {
+// Rows per CTA: a whole 128-row tile when tiles are plenty (two CTAs fit an
+// SM), else 64 .. 8 rows -- more CTAs, and more lane groups per row -- when few
+// tiles would leave SMs idle (KV-head sharding over several GPUs leaves each
+// rank few heads, and each query tile then has many partial slots to merge).
+int rows_per_cta(int64_t tiles) {
   const int64_t target = 2 * static_cast<int64_t>(current_sm_count());
-  int rp = kMaxRows;
-  while (rp > 8 && (rows + rp - 1) / rp < target) rp /= 2;
+  int rp = kTileRows;
+  while (rp > 8 && tiles * (kTileRows / rp) < target) rp /= 2;
   return rp;
 }
 
-template <typename T, int D>
-int launch_suffix(const SuffixParams& prm, dim3 grid, int smem, cudaStream_t stream) {
+template <typename T, int D, int NK>
+int launch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                  const SuffixParams& prm, dim3 grid, cudaStream_t stream) {
+  using C = SCfg<D, NK>;
   static int configured = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured != dev) {
-    cudaError_t e = cudaFuncSetAttribute(suffix_merge_kernel<T, D>,
+    cudaError_t e = cudaFuncSetAttribute(suffix_merge_kernel<T, D, NK>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         SmemLayout(kMaxBlockLen, D, sizeof(T)).total);
+                                         C::kSmemBytes);
     if (e != cudaSuccess)
       return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured = dev;
   }
-  return launch_pdl(suffix_merge_kernel<T, D>, grid, dim3(kThreads), smem, stream,
-                    "suffix_merge_kernel", prm);
+  return launch_pdl(suffix_merge_kernel<T, D, NK>, grid, dim3(kThreads), C::kSmemBytes, stream,
+                    "suffix_merge_kernel", tq, tk, tv, prm);
+}
+
+template <typename T>
+int dispatch_suffix(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                    const SuffixParams& prm, int D, int NK, dim3 grid, cudaStream_t st) {
+  if (D == 128) {
+    return NK == 32 ? launch_suffix<T, 128, 32>(tq, tk, tv, prm, grid, st)
+                    : launch_suffix<T, 128, 64>(tq, tk, tv, prm, grid, st);
+  }
+  return NK == 32 ? launch_suffix<T, 64, 32>(tq, tk, tv, prm, grid, st)
+                  : launch_suffix<T, 64, 64>(tq, tk, tv, prm, grid, st);
 }
 
 struct PeerArgs {
@@ -776,29 +770,63 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
   prm.pg_sh = pa.sh;
   prm.epoch = pa.epoch;
 
-  // a unit is one (block, kv head): block_len * G rows; without level 2 the
-  // blocks do not matter and all tokens of a head form one unit
-  int64_t units_x = num_blocks, tb = block_len;
-  if (!k_local) {
-    tb = static_cast<int64_t>(num_blocks) * block_len;
-    units_x = 1;
-  }
-  if (tb * G > INT32_MAX / 2)
+  // Tiles: when block_len * G divides 128 (and G >= 2, so that a tile's keys
+  // stay within 64), a 128-row tile spans 128 / (block_len * G) whole blocks;
+  // otherwise tiles lie inside one block. Without level 2 the blocks do not
+  // matter: all tokens of a head form one group.
+  const int64_t ntok = static_cast<int64_t>(num_blocks) * block_len;
+  if (ntok * G > INT32_MAX / 2)
     return fail(D2SD_ERR_UNSUPPORTED, "d2sd_suffix_merge: too many tokens");
+  int64_t tb = block_len, kblk = 1, groups = num_blocks;
+  if (!k_local) {
+    tb = ntok;
+    groups = 1;
+  } else if (G >= 2 && tb * G < plan::kTileRows && plan::kTileRows % (tb * G) == 0) {
+    kblk = plan::kTileRows / (tb * G);
+    groups = (num_blocks + kblk - 1) / kblk;
+  }
+  const int64_t tiles_per_group = (kblk * tb * G + plan::kTileRows - 1) / plan::kTileRows;
   prm.block_len = static_cast<int32_t>(tb);
-  prm.rows_per_unit = static_cast<int32_t>(tb * G);
-  const int rp = rows_per_cta(units_x * num_kv_heads * tb * G);
+  prm.tile_blocks = static_cast<int32_t>(kblk);
+  prm.num_tokens = static_cast<int32_t>(ntok);
+  const int rp = rows_per_cta(groups * num_kv_heads * tiles_per_group);
   prm.rows_per_cta = rp;
-  const dim3 grid(static_cast<unsigned>(units_x), static_cast<unsigned>(num_kv_heads),
-                  static_cast<unsigned>((tb * G + rp - 1) / rp));
-  const int esz = 2;  // bf16 or f16
-  const int smem = SmemLayout(k_local ? static_cast<int>(tb) : 0, head_dim, esz).total;
+  const dim3 grid(static_cast<unsigned>(groups), static_cast<unsigned>(num_kv_heads),
+                  static_cast<unsigned>(tiles_per_group * (plan::kTileRows / rp)));
+  const int NK = kblk * tb <= 32 ? 32 : 64;  // keys of a tile (its group's tokens)
+
+  CUtensorMap tq, tk, tv;
+  std::memset(&tq, 0, sizeof(tq));
+  std::memset(&tk, 0, sizeof(tk));
+  std::memset(&tv, 0, sizeof(tv));
+  if (k_local) {
+    const CUtensorMapDataType tdt =
+        dtype == D2SD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    {
+      const uint64_t dims[3] = {static_cast<uint64_t>(head_dim),
+                                static_cast<uint64_t>(num_qo_heads), static_cast<uint64_t>(ntok)};
+      const uint64_t str[2] = {static_cast<uint64_t>(q_stride_head) * 2,
+                               static_cast<uint64_t>(q_stride_token) * 2};
+      const uint32_t box[3] = {64, static_cast<uint32_t>(G), static_cast<uint32_t>(128 / G)};
+      int rc = encode_tensor_map(&tq, tdt, q, 3, dims, str, box, "q");
+      if (rc) return rc;
+    }
+    {
+      const uint64_t dims[3] = {static_cast<uint64_t>(head_dim),
+                                static_cast<uint64_t>(num_kv_heads), static_cast<uint64_t>(ntok)};
+      const uint64_t str[2] = {static_cast<uint64_t>(kv_stride_head) * 2,
+                               static_cast<uint64_t>(kv_stride_token) * 2};
+      const uint32_t box[3] = {64, 1, static_cast<uint32_t>(NK)};
+      int rc = encode_tensor_map(&tk, tdt, k_local, 3, dims, str, box, "k_local");
+      if (rc) return rc;
+      rc = encode_tensor_map(&tv, tdt, v_local, 3, dims, str, box, "v_local");
+      if (rc) return rc;
+    }
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == D2SD_DTYPE_BF16)
-    return head_dim == 128 ? launch_suffix<__nv_bfloat16, 128>(prm, grid, smem, st)
-                           : launch_suffix<__nv_bfloat16, 64>(prm, grid, smem, st);
-  return head_dim == 128 ? launch_suffix<__half, 128>(prm, grid, smem, st)
-                         : launch_suffix<__half, 64>(prm, grid, smem, st);
+    return dispatch_suffix<__nv_bfloat16>(tq, tk, tv, prm, head_dim, NK, grid, st);
+  return dispatch_suffix<__half>(tq, tk, tv, prm, head_dim, NK, grid, st);
 }
 }  // namespace
 }  // namespace d2sd

@@ -146,12 +146,15 @@ struct SCfg {
   static constexpr int kSmemQ = 0;
   static constexpr int kSmemK = kQBytes;
   static constexpr int kSmemV = kSmemK + kKVBytes;
-  static constexpr int kSmemBar = kSmemV + kKVBytes;
+  // the staged local output [128][D + 4] fp32 reuses (and may extend) the
+  // Q/K/V region once both MMAs have completed
+  static constexpr int kStageRow = D + 4;
+  static constexpr int kStageBytes = kTileRows * kStageRow * 4;
+  static constexpr int kRegion =
+      kSmemV + kKVBytes > kStageBytes ? kSmemV + kKVBytes : kStageBytes;
+  static constexpr int kSmemBar = (kRegion + 63) / 64 * 64;
   static constexpr int kSmemMeta = kSmemBar + 64;
   static constexpr int kSmemBytes = kSmemMeta + kTileRows * 32 + 1024;  // + align slack
-  static constexpr int kStageRow = D + 8;  // bf16 row of the staged local output
-  // the staged local output [128][D + 8] bf16 reuses the Q/K/V region
-  static_assert(kTileRows * kStageRow * 2 <= kSmemBar, "stage does not fit");
 };
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -179,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   RowMeta* meta = reinterpret_cast<RowMeta*>(smem + C::kSmemMeta);
-  T* stage = reinterpret_cast<T*>(smem + C::kSmemQ);  // reuses Q/K/V after the MMAs
+  float* stage = reinterpret_cast<float*>(smem + C::kSmemQ);  // over Q/K/V after the MMAs
 
   const int gx = blockIdx.x, h = blockIdx.y;
   // 128-row tile rt of token group gx, CTA part `part` = rows [part*RP, part*RP + RP)
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
-  // ---- phase 1b: this CTA's rows of the local O, normalised, into the bf16
+  // ---- phase 1b: this CTA's rows of the local O, normalised, into the fp32
   // stage over the Q/K/V tiles (free once both MMAs completed). Warp w (< 4)
   // owns TMEM lanes [32w, 32w + 32); it takes part if they meet the CTA's rows ----
   if (warp < 4 && warp * 32 < RP * (part + 1) && warp * 32 + 32 > RP * part) {
@@ -352,13 +355,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t o[32];
         tmem_ld32_wait(lane_base + 128 + c * 32, o);
         if (!mine) continue;
-        uint4* dst = reinterpret_cast<uint4*>(stage + lr * SP + c * 32);
+        float4* dst = reinterpret_cast<float4*>(stage + lr * SP + c * 32);
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          dst[e] = make_uint4(Fmt<T>::pack(__uint_as_float(o[8 * e]) * sc, __uint_as_float(o[8 * e + 1]) * sc),
-                              Fmt<T>::pack(__uint_as_float(o[8 * e + 2]) * sc, __uint_as_float(o[8 * e + 3]) * sc),
-                              Fmt<T>::pack(__uint_as_float(o[8 * e + 4]) * sc, __uint_as_float(o[8 * e + 5]) * sc),
-                              Fmt<T>::pack(__uint_as_float(o[8 * e + 6]) * sc, __uint_as_float(o[8 * e + 7]) * sc));
+        for (int e = 0; e < 8; ++e)
+          dst[e] = make_float4(__uint_as_float(o[4 * e]) * sc, __uint_as_float(o[4 * e + 1]) * sc,
+                               __uint_as_float(o[4 * e + 2]) * sc, __uint_as_float(o[4 * e + 3]) * sc);
       }
     }
   }
@@ -464,13 +465,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int e = 0; e < CPL; ++e) acc[e] = 0.f;
     if (sg == 0) {  // the local and dense-prefix states enter once per row
       if (p.has_local && live) {
-        const uint4* st = reinterpret_cast<const uint4*>(stage + lr * SP + j8 * CPL);
+        const float4* st = reinterpret_cast<const float4*>(stage + lr * SP + j8 * CPL);
 #pragma unroll
-        for (int c = 0; c < VEC; ++c) {
-          float f[8];
-          Fmt<T>::unpack(st[c], f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[c * 8 + e] = w_l * f[e];
+        for (int e = 0; e < CPL / 4; ++e) {
+          const float4 x = st[e];
+          acc[4 * e] = w_l * x.x;
+          acc[4 * e + 1] = w_l * x.y;
+          acc[4 * e + 2] = w_l * x.z;
+          acc[4 * e + 3] = w_l * x.w;
         }
       }
       if (po) {

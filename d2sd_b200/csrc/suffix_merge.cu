@@ -19,9 +19,8 @@
 //            warps 0-3 (thread = row = TMEM lane) mask (same block, and causal,
 //            full or a custom bitmask inside it), exponentiate and write P back
 //            to TMEM; thread 0 issues O = P V (A from TMEM, V MN-major). The
-//            CTA's rows of O, normalised, are staged in bf16 over the Q tile --
-//            the precision in which the reference's level-2 output reaches its
-//            merge -- with their base-2 LSEs.
+//            CTA's rows of O, normalised, are staged in fp32 over the Q/K/V
+//            tiles, with their base-2 LSEs.
 //   phase 2  (after the previous kernel -- kernel (a) -- has completed) 8-lane
 //            groups merge each row's local state with every partial state
 //            kernel (a) wrote for its query tile (or a dense prefix state),
@@ -643,7 +642,7 @@ namespace {
 // tiles would leave SMs idle (KV-head sharding over several GPUs leaves each
 // rank few heads, and each query tile then has many partial slots to merge).
 int rows_per_cta(int64_t tiles) {
-  const int64_t target = 2 * static_cast<int64_t>(current_sm_count());
+  const int64_t target = current_sm_count();
   int rp = kTileRows;
   while (rp > 8 && tiles * (kTileRows / rp) < target) rp /= 2;
   return rp;

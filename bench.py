@@ -203,20 +203,38 @@ class Ctx:
         self.barrier()
         return self.max(e0.elapsed_time(e1))
 
-    def timed_region(self, fn, steps: int, warmup: int, before=None):
-        """Warm-up, then exactly `steps` calls timed with the clocks sampled
-        (`before` runs between the two); returns (total ms max over ranks,
-        clocks)."""
-        for i in range(max(3, warmup)):
-            fn(i)
-        self.barrier()
-        if before is not None:
-            before()
-        sampler = ClockSampler(self.local_rank)
-        sampler.start()
-        time.sleep(0.3)
-        ms = self.time_ms(fn, steps)
-        return ms, sampler.stop()
+
+def timed_steps(ctx: Ctx, step, steps: int, warmup: int, before=None, graph: bool = True):
+    """Warm-up steps run eagerly; then the step is captured into a CUDA graph
+    (two steps per graph on several GPUs, so that each exchange's epoch parity
+    still alternates from replay to replay) and exactly `steps` steps are timed
+    by replaying it, as a serving loop would run a fixed-shape step; the
+    kernels are the same, the per-launch host overhead is gone. Returns (total
+    ms max over ranks, clocks, graph)."""
+    import torch
+    for _ in range(max(3, warmup)):
+        step()
+    ctx.barrier()
+    per = 2 if ctx.world > 1 else 1
+    g = None
+    run = lambda i: step()  # noqa: E731
+    reps = steps
+    if graph and steps % per == 0:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(per):
+                step()
+        g.replay()  # one untimed replay
+        ctx.barrier()
+        run = lambda i: g.replay()  # noqa: E731
+        reps = steps // per
+    if before is not None:
+        before()
+    sampler = ClockSampler(ctx.local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    ms = ctx.time_ms(run, reps)
+    return ms, sampler.stop(), g
 
 
 def check_status(ctx: Ctx, what: str, words: dict) -> dict:
@@ -639,9 +657,11 @@ def bench_cfg3(ctx: Ctx) -> dict:
     c = Cfg3(ctx)
     L, N = c.L, c.N
     before = c.px.reset_stats if c.px is not None else None
-    ms_total, clocks = ctx.timed_region(lambda i: c.step(), a.steps, a.warmup, before)
+    ms_total, clocks, graph = timed_steps(ctx, c.step, a.steps, a.warmup, before,
+                                          graph=a.exchange == "peer" or ctx.world == 1)
     ms_step = ms_total / a.steps
     xwait = c.px.wait_stats() if c.px is not None else None
+    del graph
     # per-kernel events on one extra step after the timed region: an event
     # between two kernels keeps the second from starting early (the programmatic
     # launch overlap), so this marked step runs slower than the timed ones
@@ -703,6 +723,8 @@ def bench_cfg3(ctx: Ctx) -> dict:
         "acceptance_length": acc_len,
     }
     out = {"value": N * a.steps / (ms_total / 1e3), "ms_per_step": ms_step,
+           "step_timing": ("the step captured into a CUDA graph (two steps per graph on several "
+                           "GPUs) and replayed; warm-up, per-kernel events and e2e run eagerly"),
            "us_per_layer": (ms_step - c_avg - d_avg) / L * 1e3, "status": statuses,
            "roofline": roofline, "kernels": kernels, "clocks": clocks,
            "gpu_launches": a.steps * (2 * L + 2)}
@@ -882,7 +904,8 @@ def bench_cfg4(ctx: Ctx) -> dict:
     a = ctx.a
     c = Cfg4(ctx)
     L, N, B, T, Hq, Hk, D = c.L, c.N, c.B, c.T, c.Hq, c.Hk, c.D
-    ms_total, clocks = ctx.timed_region(lambda i: c.step(), a.steps, a.warmup)
+    ms_total, clocks, graph = timed_steps(ctx, c.step, a.steps, a.warmup)
+    del graph
     k = marked_kernel_ms(ctx, c)
     a_b2b = ctx.time_ms(lambda i: c.plan.run_prefix(
         c.q[i % L], c.pool.k[i % L], c.pool.v[i % L], c.pool.kv_layout, c.scale,
@@ -1088,7 +1111,8 @@ def bench_cfg5(ctx: Ctx) -> dict:
     c = Cfg5(ctx)
     L, N, hq, hk, D, P = c.L, c.N, c.hq, c.hk, c.D, c.P
     before = c.px.reset_stats if c.px is not None else None
-    ms_total, clocks = ctx.timed_region(lambda i: c.step(), a.steps, a.warmup, before)
+    ms_total, clocks, graph = timed_steps(ctx, c.step, a.steps, a.warmup, before)
+    del graph
     xwait = c.px.wait_stats() if c.px is not None else None
     k = marked_kernel_ms(ctx, c)
     full = [l for l in range(L) if not c.sliding[l]]
@@ -1192,7 +1216,8 @@ def bench_cfg2(ctx: Ctx) -> dict:
         logits, _, _ = cascade_verify_forward(model, input_ids, pos, cache, True)
         ver.launch(logits.view(1, B, T, V), input_ids.view(1, B, T))
 
-    ms_total, clocks = ctx.timed_region(step, a.steps, a.warmup)
+    ms_total, clocks, graph = timed_steps(ctx, lambda: step(0), a.steps, a.warmup)
+    del graph
     ms = ms_total / a.steps
     # the attention kernels alone on the same shapes (36 x (a)+(b)) for the share
     Hq, Hk, D = c["qo_heads"], c["kv_heads"], c["head_dim"]
@@ -1216,6 +1241,7 @@ def bench_cfg2(ctx: Ctx) -> dict:
     out = {
         "metric": "verified tokens/s", "unit": "tokens/s", "value": B * T / (ms / 1e3),
         "ms_per_step": ms, "n_gpus": 1, "scaling": "strong", "clocks": clocks,
+        "timing": "the step captured once into a CUDA graph and replayed (the HF reference path below runs eagerly, as the reference does)",
         "workload": (f"BASELINE config 2: Qwen3-8B architecture, random init (std 0.02), bf16, "
                      f"{c['layers']} layers, hidden {c['hidden']}, {Hq}/{Hk} heads, D {D}, vocab "
                      f"{V}; prefix {P} random ids (HF prefill into a DynamicCache); one "

@@ -45,6 +45,11 @@ def _prefix(past_key_values, idx):
     return layer.keys[0], layer.values[0], "hnd", layer.keys.shape[2], None
 
 
+# Plans by shape, kept across calls: a decode loop (or a CUDA graph capture
+# after one warm-up call) then builds no plan and copies nothing to the device.
+_plans: dict = {}
+
+
 @torch.no_grad()
 def cascade_verify_forward(target_model, input_ids: torch.Tensor, position_ids: torch.Tensor,
                            past_key_values, output_hidden_states: bool = True,
@@ -59,7 +64,6 @@ def cascade_verify_forward(target_model, input_ids: torch.Tensor, position_ids: 
     cos_t, sin_t = cos[0].contiguous(), sin[0].contiguous()
     all_hidden = [hidden] if output_hidden_states else None
     new_kv_list = []
-    plans: dict = {}
 
     for layer_idx, layer in enumerate(model.layers):
         residual = hidden
@@ -85,11 +89,13 @@ def cascade_verify_forward(target_model, input_ids: torch.Tensor, position_ids: 
         keys, values, kv_layout, P, page_table = _prefix(past_key_values, layer_idx)
         window = getattr(attn, "sliding_window", None)
         kv_start = P - window if (window is not None and P > window) else 0
-        key = (P, kv_start, Hq, Hk, D)
-        plan = plans.get(key)
+        key = (bsz * seq_len, P, kv_start, Hq, Hk, D, str(q.device))
+        plan = _plans.get(key)
         if plan is None:
             plan = CascadePlan([Request(bsz * seq_len, 0, kv_start, P)], Hq, Hk, D, q.device)
-            plans[key] = plan
+            if len(_plans) > 256:
+                _plans.clear()
+            _plans[key] = plan
         sinks = attn.sinks.float() if is_gpt_oss else None
         out, _ = cascade_attention(q.transpose(1, 2), k_new.transpose(1, 2),
                                    v_new.transpose(1, 2), keys, values, kv_layout, P,

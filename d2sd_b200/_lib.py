@@ -74,6 +74,9 @@ SIGNATURES = {
                                          i64, vp, vp]),
     "d2sd_commit_kv_batch": (i32, [vp, i32, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64,
                                    i64, i64, i32, i32, vp, vp, vp, vp, vp]),
+    "d2sd_cascade_attention_f32": (i32, [vp, i64, i64, vp, vp, i64, i64, i32, i32, vp, vp, i64,
+                                         i64, i32, i32, i32, vp, vp, i64, i64, vp, i64, vp, i32,
+                                         vp, i64, i64, vp, i64, i32, i32, i32, f32, vp]),
     "d2sd_commit_kv": (i32, [vp, i32, i32, i32, i32, i32, i64, i64, i64, i64, i64, i64, i32, i32,
                              vp, vp, vp, i64, vp]),
     "d2sd_qk_norm_rope": (i32, [vp, i64, i64, vp, i64, i64, vp, i64, i64, vp, i64, i64, i32, i32,

@@ -113,7 +113,8 @@ def cascade_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
     (see ops.kv_view) holding ``kv_len`` positions. ``sliding_window`` keeps only
     the last window prefix keys (generation/verification.py:130-135);
     ``shared_tokens`` > 0 declares that all branches share their first tokens,
-    so their prefix attention is computed once. Returns (out [B, T, Hq, D],
+    so their prefix attention is computed once. fp32 q/k/v (a contiguous
+    "nhd" or "hnd" prefix) take the fp32 kernel (d2sd_cascade_attention_f32). Returns (out [B, T, Hq, D],
     lse [B, T, Hq] base 2), written into ``out``/``lse`` when given. Kernel (a)
     reports a wait time-out in ``plan.status``, kernel (b) in ``status`` (an
     int32 device tensor, optional).
@@ -122,6 +123,9 @@ def cascade_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
     Hk = k_new.shape[2]
     scale = D ** -0.5 if sm_scale is None else float(sm_scale)
     kv_start = max(0, kv_len - sliding_window) if sliding_window is not None else 0
+    if q.dtype == torch.float32:
+        return _cascade_f32(q, k_new, v_new, k_cache, v_cache, kv_layout, kv_len, kv_start,
+                            causal, scale, sinks, sink_mode, custom_mask, out, lse)
     if shared_tokens:
         n_u = shared_tokens + B * (T - shared_tokens)
         q_pref = torch.cat([q[0, :shared_tokens], q[:, shared_tokens:].reshape(-1, Hq, D)], 0)
@@ -146,4 +150,30 @@ def cascade_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                      prefix_token=ptok, sinks=sinks,
                      sink_mode=_SINKS[sink_mode] if sinks is not None else _lib.SINK_NONE,
                      status=status)
+    return out, lse
+
+
+def _cascade_f32(q, k_new, v_new, k_cache, v_cache, kv_layout, kv_len, kv_start, causal, scale,
+                 sinks, sink_mode, custom_mask, out, lse):
+    """The fp32 form of ``cascade_attention`` (one launch of the SIMT fp32
+    kernel: prefix keys, the block's own keys and the sinks in fp32)."""
+    B, T, Hq, D = q.shape
+    Hk = k_new.shape[2]
+    if kv_layout == "nhd":
+        kp, vp = k_cache[:kv_len], v_cache[:kv_len]
+    elif kv_layout == "hnd":
+        kp, vp = k_cache[:, :kv_len].transpose(0, 1), v_cache[:, :kv_len].transpose(0, 1)
+    else:
+        raise NotImplementedError("the fp32 cascade reads a contiguous nhd/hnd prefix")
+    if out is None:
+        out = torch.empty(B, T, Hq, D, dtype=torch.float32, device=q.device)
+    if lse is None:
+        lse = torch.empty(B, T, Hq, dtype=torch.float32, device=q.device)
+    mode = _MASKS["custom" if custom_mask is not None else ("causal" if causal else "none")]
+    ops.cascade_attention_f32(
+        q.reshape(B * T, Hq, D), out.view(B * T, Hq, D), lse.view(B * T, Hq), num_blocks=B,
+        block_len=T, num_kv_heads=Hk, sm_scale=scale, k_prefix=kp if kv_len else None,
+        v_prefix=vp if kv_len else None, kv_start=kv_start, k_local=k_new.reshape(B * T, Hk, D),
+        v_local=v_new.reshape(B * T, Hk, D), mask_mode=mode, custom_mask=custom_mask, sinks=sinks,
+        sink_mode=_SINKS[sink_mode] if sinks is not None else _lib.SINK_NONE)
     return out, lse

@@ -52,9 +52,21 @@ def single_prefill_with_kv_cache(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
     scale = D ** -0.5 if sm_scale is None else float(sm_scale)
     out = torch.empty(N, Hq, D, dtype=q.dtype, device=q.device)
     lse = torch.empty(N, Hq, dtype=torch.float32, device=q.device)
+    kk = k if layout == "nhd" else k.transpose(0, 1)
+    vv = v if layout == "nhd" else v.transpose(0, 1)
+    if q.dtype == torch.float32:  # fp32 end to end (d2sd_cascade_attention_f32)
+        if N == P and N <= 64:
+            ops.cascade_attention_f32(q, out, lse, num_blocks=1, block_len=N, num_kv_heads=Hk,
+                                      sm_scale=scale, k_local=kk, v_local=vv,
+                                      mask_mode=_lib.MASK_CAUSAL if causal else _lib.MASK_NONE)
+        elif not causal:
+            ops.cascade_attention_f32(q, out, lse, num_blocks=1, block_len=N, num_kv_heads=Hk,
+                                      sm_scale=scale, k_prefix=kk if P else None,
+                                      v_prefix=vv if P else None)
+        else:
+            raise NotImplementedError("causal prefill with qo_len != kv_len is outside D2-SD's path")
+        return (out, lse) if return_lse else out
     if N == P and N <= 64:
-        kk = k if layout == "nhd" else k.transpose(0, 1)
-        vv = v if layout == "nhd" else v.transpose(0, 1)
         ops.suffix_merge(q, kk, vv, out, lse, num_blocks=1, block_len=N, num_qo_heads=Hq,
                          num_kv_heads=Hk, sm_scale=scale,
                          mask_mode=_lib.MASK_CAUSAL if causal else _lib.MASK_NONE)

@@ -226,6 +226,44 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
     exchange.next_epoch()  # only a launched call advances the epoch
 
 
+def cascade_attention_f32(q: torch.Tensor, out: torch.Tensor, lse: torch.Tensor | None, *,
+                          num_blocks: int, block_len: int, num_kv_heads: int, sm_scale: float,
+                          k_prefix: torch.Tensor | None = None,
+                          v_prefix: torch.Tensor | None = None, kv_start: int = 0,
+                          k_local: torch.Tensor | None = None, v_local: torch.Tensor | None = None,
+                          mask_mode: int = _lib.MASK_CAUSAL,
+                          custom_mask: torch.Tensor | None = None,
+                          prefix_out: torch.Tensor | None = None,
+                          prefix_lse: torch.Tensor | None = None,
+                          sinks: torch.Tensor | None = None, sink_mode: int = _lib.SINK_NONE) -> None:
+    """fp32 cascade attention (d2sd_cascade_attention_f32). Token-major views:
+    q/out [tokens, Hq, D]; k/v_prefix [P, Hk, D] (any token/head strides);
+    k/v_local [tokens, Hk, D]; prefix_out [tokens, Hq, D] and prefix_lse
+    [tokens, Hq] (base 2) for a dense prefix state; lse [tokens, Hq]."""
+    ts = (q, out, k_prefix, v_prefix, k_local, v_local, prefix_out)
+    dev = _require_cuda(*ts, lse, custom_mask, prefix_lse, sinks)
+    for t in ts + (lse, prefix_lse, sinks):
+        if t is not None and (t.dtype != torch.float32 or t.stride(-1) != 1):
+            raise ValueError("the fp32 cascade takes fp32 tensors with a contiguous last axis")
+    if (k_prefix is None) != (v_prefix is None) or (k_local is None) != (v_local is None):
+        raise ValueError("keys and values go together")
+    if k_prefix is not None and k_prefix.stride() != v_prefix.stride():
+        raise ValueError("k_prefix and v_prefix must share strides")
+    if k_local is not None and k_local.stride() != v_local.stride():
+        raise ValueError("k_local and v_local must share strides")
+    N, Hq, D = q.shape
+    P = 0 if k_prefix is None else k_prefix.shape[0]
+    st = lambda t, i: t.stride(i) if t is not None else 0  # noqa: E731
+    check(load().d2sd_cascade_attention_f32(
+        q.data_ptr(), q.stride(0), q.stride(1), _ptr(k_prefix), _ptr(v_prefix), st(k_prefix, 0),
+        st(k_prefix, 1), P, int(kv_start), _ptr(k_local), _ptr(v_local), st(k_local, 0),
+        st(k_local, 1), int(num_blocks), int(block_len), int(mask_mode), _ptr(custom_mask),
+        _ptr(prefix_out), st(prefix_out, 0), st(prefix_out, 1), _ptr(prefix_lse),
+        st(prefix_lse, 0), _ptr(sinks), int(sink_mode), out.data_ptr(), out.stride(0),
+        out.stride(1), _ptr(lse), st(lse, 0), Hq, int(num_kv_heads), D, float(sm_scale),
+        _stream(dev)), "d2sd_cascade_attention_f32")
+
+
 def merge_state(v: torch.Tensor, s: torch.Tensor, v_other: torch.Tensor,
                 s_other: torch.Tensor) -> None:
     """In-place (v, s) <- merge((v, s), (v_other, s_other)); v [n, H, D], s [n, H]."""

@@ -24,8 +24,8 @@ from . import _lib, ops
 class CascadeGraphRunner:
     def __init__(self, block_size: int, num_heads: int, num_kv_heads: int, head_dim: int,
                  dtype: torch.dtype, device: torch.device, sm_scale: float, causal: bool):
-        if dtype not in (torch.bfloat16, torch.float16):
-            raise ValueError("CascadeGraphRunner: dtype must be bf16 or fp16")
+        if dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise ValueError("CascadeGraphRunner: dtype must be bf16, fp16 or fp32")
         if num_heads % num_kv_heads:
             raise ValueError("num_heads must be a multiple of num_kv_heads")
         self.block_size = block_size
@@ -57,6 +57,13 @@ class CascadeGraphRunner:
         def tok(t):  # [bsz, T, ...] -> [bsz*T, ...]; a view when the dims merge
             return t.flatten(0, 1) if _flat_ok(t) else t.reshape(bsz * T, *t.shape[2:])
 
+        if self.dtype == torch.float32:  # fp32 end to end (d2sd_cascade_attention_f32)
+            ops.cascade_attention_f32(
+                tok(q_local), tok(out_shared), tok(lse_shared), num_blocks=bsz, block_len=T,
+                num_kv_heads=Hk, sm_scale=self.sm_scale, k_local=tok(k_local),
+                v_local=tok(v_local), mask_mode=_lib.MASK_CAUSAL if self.causal else _lib.MASK_NONE,
+                prefix_out=tok(out_shared), prefix_lse=tok(lse_shared))
+            return
         ops.suffix_merge(tok(q_local), tok(k_local), tok(v_local), tok(out_shared),
                          tok(lse_shared), num_blocks=bsz, block_len=T, num_qo_heads=H,
                          num_kv_heads=Hk, sm_scale=self.sm_scale,

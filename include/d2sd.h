@@ -17,6 +17,8 @@
  *       :52-60: per-branch single_prefill + merge_state_in_place), the loop at
  *       generation/verification.py:158-165 and the GPT-OSS sink rescale at
  *       generation/verification.py:173-176.
+ *   d2sd_cascade_attention_f32
+ *       the same cascade in fp32 (BASELINE config 1's fp32 contract).
  *   d2sd_merge_state
  *       flashinfer.merge_state_in_place(v, s, v_other, s_other)
  *       model/cascade_graph.py:58-60, generation/verification.py:163-165.
@@ -416,6 +418,33 @@ int d2sd_commit_kv_batch(const void* const* layer_ptrs, int32_t num_layers,
                          const int32_t* page_table_offset,
                          const int32_t* accept_results,
                          const int32_t* cache_lens, void* stream);
+
+/* The two-level cascade verify attention in fp32 (the
+ * reference's fp32 path, generation/verification.py:127-176 with a float32
+ * target, and its CPU torch.sdpa form), for rows that need fp32 end to end
+ * instead of the bf16 tensor-core kernels. Each query row (token t of block
+ * t / block_len, query head h, kv head h / G) attends the prefix keys
+ * [kv_start, prefix_len) of k_prefix/v_prefix ([prefix_len, Hk, D], token and
+ * head strides; may be NULL when prefix_len is 0) and the tokens of its own
+ * block in k_local/v_local ([tokens, Hk, D], or NULL) under mask_mode; the
+ * state is merged with a dense prefix state (prefix_out [tokens, Hq, D],
+ * prefix_lse [tokens, Hq] base 2; the CascadeGraphRunner.run form) when given,
+ * and scaled by the sink factor of sink_mode. out [tokens, Hq, D] fp32 and lse
+ * [tokens, Hq] base 2 (or NULL). Exact expf/logf, fp32 accumulation. head_dim
+ * 32, 64 or 128; block_len <= 64 with k_local. */
+int d2sd_cascade_attention_f32(
+    const float* q, int64_t q_stride_token, int64_t q_stride_head,
+    const float* k_prefix, const float* v_prefix, int64_t prefix_stride_token,
+    int64_t prefix_stride_head, int32_t prefix_len, int32_t kv_start,
+    const float* k_local, const float* v_local, int64_t local_stride_token,
+    int64_t local_stride_head, int32_t num_blocks, int32_t block_len,
+    int32_t mask_mode, const uint64_t* custom_mask, const float* prefix_out,
+    int64_t prefix_out_stride_token, int64_t prefix_out_stride_head,
+    const float* prefix_lse, int64_t prefix_lse_stride_token,
+    const float* sinks, int32_t sink_mode, float* out, int64_t out_stride_token,
+    int64_t out_stride_head, float* lse, int64_t lse_stride_token,
+    int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+    float sm_scale, void* stream);
 
 /* Per-head RMSNorm (optional) and rotary embedding of the block's q and k in
  * one launch, with the 16-bit roundings of the reference's eager expressions:

@@ -49,10 +49,10 @@ SIGNATURES = {
     "d2sd_partial_slot_bytes": (i64, [i32]),
     "d2sd_prefix_attention": (i32, [vp, i64, i64, i64, vp, vp, i64, i64, i64, i32, i32, i64, vp,
                                     vp, i32, i32, i32, f32, vp, i32, vp, i64, vp, vp]),
-    "d2sd_suffix_merge": (i32, [vp, i64, i64, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp,
+    "d2sd_suffix_merge": (i32, [vp, i64, i64, i64, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp, vp,
                                 vp, i64, i64, vp, i64, vp, i64, i64, vp, i64, vp, i32, i32, i32,
                                 i32, i32, f32, vp, vp]),
-    "d2sd_suffix_merge_gather": (i32, [vp, i64, i64, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp,
+    "d2sd_suffix_merge_gather": (i32, [vp, i64, i64, i64, vp, vp, i64, i64, i32, i32, i32, vp, vp, vp,
                                        vp, vp, i64, i64, vp, i64, vp, i64, i64, vp, i64, vp, i32,
                                        i32, i32, i32, i32, f32, vp, vp, i32, i32, i32, i64, i64,
                                        i64, vp, vp]),

@@ -252,8 +252,14 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive_expect_tx(&bars[0], C::kQBytes + 2 * C::kKVBytes);
 #pragma unroll
       for (int pn = 0; pn < C::kPanels; ++pn) {
-        tma_load_3d(smem + C::kSmemQ + pn * kPanelQ, &tm_q, &bars[0], pn * 64, h * G,
-                    gt0 + rt * (kTileRows / G));
+        if (p.tile_blocks > 1) {  // one box per block of the tile (its T*G rows)
+          for (int bi = 0; bi < p.tile_blocks; ++bi)
+            tma_load_4d(smem + C::kSmemQ + pn * kPanelQ + bi * TB * G * 128, &tm_q, &bars[0],
+                        pn * 64, h * G, 0, gx * p.tile_blocks + bi);
+        } else {
+          tma_load_4d(smem + C::kSmemQ + pn * kPanelQ, &tm_q, &bars[0], pn * 64, h * G,
+                      rt * (kTileRows / G), gx);
+        }
         tma_load_3d(smem + C::kSmemK + pn * C::kPanelKV, &tm_k, &bars[0], pn * 64, h, gt0);
         tma_load_3d(smem + C::kSmemV + pn * C::kPanelKV, &tm_v, &bars[0], pn * 64, h, gt0);
       }
@@ -686,7 +692,7 @@ struct PeerArgs {
 };
 
 int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_head,
-                      const void* k_local, const void* v_local, int64_t kv_stride_token,
+                      int64_t q_stride_block, const void* k_local, const void* v_local, int64_t kv_stride_token,
                       int64_t kv_stride_head, int32_t num_blocks, int32_t block_len,
                       int32_t mask_mode, const uint64_t* custom_mask, const void* partial,
                       const int32_t* plan, const int32_t* prefix_token, const void* prefix_out,
@@ -726,7 +732,8 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
   if (partial && (reinterpret_cast<uintptr_t>(partial) & 15u))
     return fail(D2SD_ERR_INVALID_ARGUMENT, "d2sd_suffix_merge: partial must be 16-byte aligned");
   if (k_local && (!aligned16(q) || !aligned16(k_local) || !aligned16(v_local) ||
-                  q_stride_token % 8 || q_stride_head % 8 || kv_stride_token % 8 ||
+                  q_stride_token % 8 || q_stride_head % 8 || q_stride_block % 8 ||
+                  kv_stride_token % 8 ||
                   kv_stride_head % 8))
     return fail(D2SD_ERR_INVALID_ARGUMENT,
                 "d2sd_suffix_merge: q/k/v must be 16-byte aligned with strides multiple of 8");
@@ -782,7 +789,8 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
   if (!k_local) {
     tb = ntok;
     groups = 1;
-  } else if (G >= 2 && tb * G < plan::kTileRows && plan::kTileRows % (tb * G) == 0) {
+  } else if (G >= 2 && tb * G < plan::kTileRows && plan::kTileRows % (tb * G) == 0 &&
+             (tb * G) % 8 == 0) {  // each block's rows start on a 1024-byte swizzle period
     kblk = plan::kTileRows / (tb * G);
     groups = (num_blocks + kblk - 1) / kblk;
   }
@@ -804,12 +812,19 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
     const CUtensorMapDataType tdt =
         dtype == D2SD_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     {
-      const uint64_t dims[3] = {static_cast<uint64_t>(head_dim),
-                                static_cast<uint64_t>(num_qo_heads), static_cast<uint64_t>(ntok)};
-      const uint64_t str[2] = {static_cast<uint64_t>(q_stride_head) * 2,
-                               static_cast<uint64_t>(q_stride_token) * 2};
-      const uint32_t box[3] = {64, static_cast<uint32_t>(G), static_cast<uint32_t>(128 / G)};
-      int rc = encode_tensor_map(&tq, tdt, q, 3, dims, str, box, "q");
+      // q as [blocks, block_len, Hq, D] with its own block stride: token-major
+      // tensors and per-block views (a [B, Hq, T, D] tensor transposed to
+      // [B, T, Hq, D]) alike are read in place
+      const int64_t qsb = q_stride_block ? q_stride_block : block_len * q_stride_token;
+      const uint64_t dims[4] = {static_cast<uint64_t>(head_dim),
+                                static_cast<uint64_t>(num_qo_heads),
+                                static_cast<uint64_t>(block_len), static_cast<uint64_t>(num_blocks)};
+      const uint64_t str[3] = {static_cast<uint64_t>(q_stride_head) * 2,
+                               static_cast<uint64_t>(q_stride_token) * 2,
+                               static_cast<uint64_t>(qsb) * 2};
+      const uint32_t box[4] = {64, static_cast<uint32_t>(G),
+                               static_cast<uint32_t>(kblk > 1 ? block_len : 128 / G), 1};
+      int rc = encode_tensor_map(&tq, tdt, q, 4, dims, str, box, "q");
       if (rc) return rc;
     }
     {
@@ -833,7 +848,7 @@ int suffix_merge_impl(const void* q, int64_t q_stride_token, int64_t q_stride_he
 }  // namespace d2sd
 
 extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t q_stride_head,
-                                 const void* k_local, const void* v_local, int64_t kv_stride_token,
+                                 int64_t q_stride_block, const void* k_local, const void* v_local, int64_t kv_stride_token,
                                  int64_t kv_stride_head, int32_t num_blocks, int32_t block_len,
                                  int32_t mask_mode, const uint64_t* custom_mask,
                                  const void* partial, const int32_t* plan,
@@ -845,7 +860,8 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
                                  int32_t sink_mode, int32_t num_qo_heads, int32_t num_kv_heads,
                                  int32_t head_dim, int32_t dtype, float sm_scale,
                                  int32_t* status, void* stream) {
-  return d2sd::suffix_merge_impl(q, q_stride_token, q_stride_head, k_local, v_local,
+  return d2sd::suffix_merge_impl(q, q_stride_token, q_stride_head, q_stride_block, k_local,
+                                 v_local,
                                  kv_stride_token, kv_stride_head, num_blocks, block_len, mask_mode,
                                  custom_mask, partial, plan, prefix_token, prefix_out,
                                  prefix_out_stride_token, prefix_out_stride_head, prefix_lse,
@@ -856,8 +872,9 @@ extern "C" int d2sd_suffix_merge(const void* q, int64_t q_stride_token, int64_t 
 }
 
 extern "C" int d2sd_suffix_merge_gather(
-    const void* q, int64_t q_stride_token, int64_t q_stride_head, const void* k_local,
-    const void* v_local, int64_t kv_stride_token, int64_t kv_stride_head, int32_t num_blocks,
+    const void* q, int64_t q_stride_token, int64_t q_stride_head, int64_t q_stride_block,
+    const void* k_local, const void* v_local, int64_t kv_stride_token, int64_t kv_stride_head,
+    int32_t num_blocks,
     int32_t block_len, int32_t mask_mode, const uint64_t* custom_mask, const void* partial,
     const int32_t* plan, const int32_t* prefix_token, const void* prefix_out,
     int64_t prefix_out_stride_token, int64_t prefix_out_stride_head, const float* prefix_lse,
@@ -887,7 +904,8 @@ extern "C" int d2sd_suffix_merge_gather(
   pa.st = peer_stride_token;
   pa.sh = peer_stride_head;
   pa.epoch = epoch;
-  return suffix_merge_impl(q, q_stride_token, q_stride_head, k_local, v_local, kv_stride_token,
+  return suffix_merge_impl(q, q_stride_token, q_stride_head, q_stride_block, k_local, v_local,
+                           kv_stride_token,
                            kv_stride_head, num_blocks, block_len, mask_mode, custom_mask, partial,
                            plan, prefix_token, prefix_out, prefix_out_stride_token,
                            prefix_out_stride_head, prefix_lse, prefix_lse_stride_token, out,

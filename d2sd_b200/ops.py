@@ -176,7 +176,8 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
                  sinks: torch.Tensor | None = None, sink_mode: int = _lib.SINK_NONE,
                  status: torch.Tensor | None = None, exchange=None) -> None:
     """Launch kernel (b). Token-major 3-D views: q/out [tokens, Hq, D],
-    k/v_local [tokens, Hk, D], lse/prefix_lse [tokens, Hq].
+    k/v_local [tokens, Hk, D], lse/prefix_lse [tokens, Hq]; q may also be a 4-D
+    [num_blocks, block_len, Hq, D] view with any block stride (read in place).
 
     exchange: a ``sharding.PeerExchange``; the merged rows then go into every
     rank's exchange buffer of this call's epoch parity at this rank's head
@@ -186,7 +187,14 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
     time-out code."""
     dev = _require_cuda(q, k_local, v_local, out, lse, custom_mask, partial, plan_dev,
                         prefix_token, prefix_out, prefix_lse, sinks, status)
-    for t in (q, k_local, v_local, out, prefix_out):
+    q_sb, q_st, q_sh = 0, 0, 0
+    if q is not None and q.dim() == 4:  # [blocks, block_len, Hq, D] with its own block stride
+        if q.shape[0] != num_blocks or q.shape[1] != block_len or q.stride(-1) != 1:
+            raise ValueError("a 4-D q must be [num_blocks, block_len, heads, head_dim]")
+        q_sb, q_st, q_sh = q.stride(0), q.stride(1), q.stride(2)
+    elif q is not None:
+        q_st, q_sh = q.stride(0), q.stride(1)
+    for t in (k_local, v_local, out, prefix_out) + ((q,) if q is not None and q.dim() == 3 else ()):
         if t is not None and (t.dim() != 3 or t.stride(-1) != 1):
             raise ValueError("token tensors must be [tokens, heads, head_dim], head_dim contiguous")
     for t in (lse, prefix_lse):
@@ -200,7 +208,7 @@ def suffix_merge(q: torch.Tensor | None, k_local: torch.Tensor | None,
     kst = k_local.stride(0) if k_local is not None else 0
     ksh = k_local.stride(1) if k_local is not None else 0
     args = (
-        _ptr(q), q.stride(0) if q is not None else 0, q.stride(1) if q is not None else 0,
+        _ptr(q), q_st, q_sh, q_sb,
         _ptr(k_local), _ptr(v_local), kst, ksh, int(num_blocks), int(block_len), int(mask_mode),
         _ptr(custom_mask), _ptr(partial), _ptr(plan_dev), _ptr(prefix_token), _ptr(prefix_out),
         prefix_out.stride(0) if prefix_out is not None else 0,

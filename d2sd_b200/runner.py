@@ -64,7 +64,9 @@ class CascadeGraphRunner:
                 v_local=tok(v_local), mask_mode=_lib.MASK_CAUSAL if self.causal else _lib.MASK_NONE,
                 prefix_out=tok(out_shared), prefix_lse=tok(lse_shared))
             return
-        ops.suffix_merge(tok(q_local), tok(k_local), tok(v_local), tok(out_shared),
+        # q is read through its own block stride (a transposed per-block view,
+        # model/dflash.py:109,124, needs no copy); k/v merge their token axes
+        ops.suffix_merge(q_local, tok(k_local), tok(v_local), tok(out_shared),
                          tok(lse_shared), num_blocks=bsz, block_len=T, num_qo_heads=H,
                          num_kv_heads=Hk, sm_scale=self.sm_scale,
                          mask_mode=_lib.MASK_CAUSAL if self.causal else _lib.MASK_NONE,

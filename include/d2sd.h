@@ -168,7 +168,11 @@ int d2sd_prefix_attention(const void* q, int64_t q_stride_token,
  * Tokens are grouped in blocks of block_len consecutive tokens (one block per
  * draft branch). q, k_local, v_local: [num_blocks*block_len, heads, head_dim]
  * with (token, head) element strides; k_local/v_local may be NULL for a pure
- * merge (no level 2).
+ * merge (no level 2). q may have its own block stride q_stride_block (0 =
+ * block_len * q_stride_token): query (block b, token t, head h) is read at
+ * b*q_stride_block + t*q_stride_token + h*q_stride_head, so a per-block view
+ * such as [B, Hq, T, D] transposed to [B, T, Hq, D] (model/dflash.py:109,124)
+ * is read in place.
  * Prefix state, one of:
  *   - partial != NULL: merged from the slots written by d2sd_prefix_attention;
  *     prefix_token[t] (device, may be NULL = identity) maps block token t to
@@ -186,7 +190,8 @@ int d2sd_prefix_attention(const void* q, int64_t q_stride_token,
  * block_len <= 64. status (device int32, may be NULL) receives a nonzero code
  * if a wait inside the kernel ran out of time. */
 int d2sd_suffix_merge(const void* q, int64_t q_stride_token,
-                      int64_t q_stride_head, const void* k_local,
+                      int64_t q_stride_head, int64_t q_stride_block,
+                      const void* k_local,
                       const void* v_local, int64_t kv_stride_token,
                       int64_t kv_stride_head, int32_t num_blocks,
                       int32_t block_len, int32_t mask_mode,
@@ -230,7 +235,8 @@ int d2sd_suffix_merge(const void* q, int64_t q_stride_token,
  * 16-byte vectors: the output bases must be 16-byte aligned and the strides
  * multiples of 8. */
 int d2sd_suffix_merge_gather(const void* q, int64_t q_stride_token,
-                             int64_t q_stride_head, const void* k_local,
+                             int64_t q_stride_head, int64_t q_stride_block,
+                             const void* k_local,
                              const void* v_local, int64_t kv_stride_token,
                              int64_t kv_stride_head, int32_t num_blocks,
                              int32_t block_len, int32_t mask_mode,

@@ -17,6 +17,8 @@ The same JSON line carries the other BASELINE configs under "configs":
         acceptance over V 201088; KV-head sharded like config 3.
   cfg2  Qwen3-8B (random init, bf16, 36 layers) full cascade_verify_forward of
         4 x 32 candidates over a 2048-token prefix (1 GPU).
+  cfg1  the fp32 single-layer case: the fp32 cascade kernel and acceptance over
+        fp32 logits (1 GPU).
 
 Multi-GPU (torchrun, one rank per GPU): KV-head sharding for configs 3 and 5
 (rank r owns Hk/N kv heads and their pages; kernel (b) stores each layer's
@@ -59,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["d2sd", "reference"], default="d2sd")
-    ap.add_argument("--configs", default="3,4,5,2",
+    ap.add_argument("--configs", default="3,4,5,2,1",
                     help="configs to run; 3 is the headline line, the others go under 'configs'")
     ap.add_argument("--layers", type=int, default=CFG3["layers"])
     ap.add_argument("--prefix", type=int, default=CFG3["prefix"])
@@ -1352,6 +1354,111 @@ def bench_cfg2(ctx: Ctx) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# config 1: the fp32 single-layer case (1 GPU)
+# ---------------------------------------------------------------------------
+CFG1 = dict(prefix=512, branches=4, block=16, qo_heads=32, kv_heads=8, head_dim=128, vocab=151936)
+
+
+def bench_cfg1(ctx: Ctx) -> dict:
+    """One fp32 cascade attention layer (d2sd_cascade_attention_f32) and the
+    acceptance over fp32 logits: BASELINE config 1 on the GPU."""
+    import torch
+
+    import d2sd_b200 as d
+    from d2sd_b200 import _lib, ops
+    a, dev, c = ctx.a, ctx.dev, CFG1
+    P, B, T, Hq, Hk, D, V = (c["prefix"], c["branches"], c["block"], c["qo_heads"],
+                             c["kv_heads"], c["head_dim"], c["vocab"])
+    g = torch.Generator(device=dev).manual_seed(0)
+    r = lambda *sh: torch.randn(*sh, generator=g, device=dev) / D ** 0.5  # noqa: E731
+    q, kn, vn, kp, vp = r(B * T, Hq, D), r(B * T, Hk, D), r(B * T, Hk, D), r(P, Hk, D), r(P, Hk, D)
+    logits = torch.randn(1, B, T, V, generator=g, device=dev)
+    ids = torch.randint(0, V, (1, B, T), generator=g, device=dev)
+    keep = torch.rand(1, B, T, generator=g, device=dev) < 0.7
+    ids[..., 1:] = torch.where(keep[..., 1:], logits.argmax(-1)[..., :-1], ids[..., 1:])
+    ids[..., 0] = ids[0, 0, 0]
+    out = torch.empty(B * T, Hq, D, device=dev)
+    lse = torch.empty(B * T, Hq, device=dev)
+    ver = d.BatchVerifier(1, B, T, V, dev)
+
+    def attn():
+        ops.cascade_attention_f32(q, out, lse, num_blocks=B, block_len=T, num_kv_heads=Hk,
+                                  sm_scale=D ** -0.5, k_prefix=kp, v_prefix=vp, k_local=kn,
+                                  v_local=vn, mask_mode=_lib.MASK_CAUSAL)
+
+    def step():
+        attn()
+        ver.launch(logits, ids)
+
+    ms_total, clocks, graph = timed_steps(ctx, step, a.steps, a.warmup)
+    del graph
+    att = graph_ms(ctx, lambda i: attn(), 10)
+    acc = graph_ms(ctx, lambda i: ver.launch(logits, ids), 10)
+    hbm, _, _, peak_src = measured_peaks()
+    out_d = {"metric": "verified tokens/s", "unit": "tokens/s", "value": B * T * a.steps / (ms_total / 1e3),
+             "ms_per_step": ms_total / a.steps, "n_gpus": 1, "scaling": "strong", "dtype": "f32",
+             "clocks": clocks,
+             "workload": (f"BASELINE config 1: fp32, seed 0, prefix {P}, {Hq}/{Hk} heads, D {D}, "
+                          f"{B} x {T} tokens causal in each branch, one layer of the fp32 cascade "
+                          f"(d2sd_cascade_attention_f32) + acceptance over [{B},{T},{V}] fp32 logits"),
+             "kernels": {"attention_f32_us": att * 1e3, "accept_us": acc * 1e3,
+                         "accept_gbs": gbs(logits.numel() * 4, acc)},
+             "roofline": {"bound": "hbm (acceptance: fp32 logits read once)", "kernel": "accept_kernel",
+                          "achieved": gbs(logits.numel() * 4, acc), "peak": hbm, "unit": "GB/s",
+                          "frac": gbs(logits.numel() * 4, acc) / hbm, "peak_source": peak_src},
+             "tolerance": "1e-5 abs/rel against the float64 oracle (tests/test_fp32_gpu.py)",
+             "gpu_launches": a.steps * 2}
+    if not a.no_e2e:
+        h_in = [t.cpu().pin_memory() for t in (q, kn, vn, kp, vp, logits, ids)]
+        d_in = (q, kn, vn, kp, vp, logits, ids)
+        h_res = torch.empty(2, dtype=torch.int32).pin_memory()
+
+        def e2e_step(_i):
+            for dt, ht in zip(d_in, h_in):
+                dt.copy_(ht, non_blocking=True)
+            step()
+            h_res.copy_(ver.result[0], non_blocking=True)
+            ctx.stream.synchronize()
+        for i in range(max(3, a.warmup)):
+            e2e_step(i)
+        e_ms = ctx.time_ms(e2e_step, a.steps) / a.steps
+        out_d["e2e"] = {"value": B * T / (e_ms / 1e3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in h_in),
+                        "d2h_bytes_per_step": 8, "ms_per_step": e_ms}
+    return out_d
+
+
+def cpu_cfg1(reps: int = 5) -> dict:
+    """Config 1 on the CPU: the fp32 tree-masked torch.sdpa layer and the walk."""
+    import numpy as np
+    import torch
+
+    from oracle import accept as OA
+    from oracle import attention as AT
+    cores = cpu_threads()
+    c = CFG1
+    P, B, T, Hq, Hk, D, V = (c["prefix"], c["branches"], c["block"], c["qo_heads"],
+                             c["kv_heads"], c["head_dim"], c["vocab"])
+    g = torch.Generator().manual_seed(0)
+    r = lambda *sh: torch.randn(*sh, generator=g) / D ** 0.5  # noqa: E731
+    q, kn, vn, kp, vp = r(B, T, Hq, D), r(B, T, Hk, D), r(B, T, Hk, D), r(P, Hk, D), r(P, Hk, D)
+    z = torch.randn(B, T, V, generator=g).numpy()
+    x = np.random.default_rng(0).integers(0, V, (B, T))
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        AT.torch_tree_sdpa(q, kn, vn, kp, vp, causal=True)
+        OA.verify_accept(z, x)
+        ts.append(time.perf_counter() - t0)
+    step = statistics.median(ts)
+    return {"value": B * T / step, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": (f"median of {reps} x [one fp32 tree-masked torch.sdpa layer (P {P}, "
+                       f"{B} x {T} tokens, {Hq}/{Hk} heads, D {D}) + the acceptance walk over "
+                       f"[{B},{T},{V}] fp32 logits] = one step"),
+            "seconds_per_step": step}
+
+
+# ---------------------------------------------------------------------------
 # the d2sd arm
 # ---------------------------------------------------------------------------
 def run_d2sd(ctx: Ctx):
@@ -1379,6 +1486,11 @@ def run_d2sd(ctx: Ctx):
         sub("cfg4", bench_cfg4, cpu_cfg4)
     if "5" in which:
         sub("cfg5", bench_cfg5, cpu_cfg5)
+    if "1" in which:
+        if world == 1:
+            sub("cfg1", bench_cfg1, cpu_cfg1)
+        else:
+            subs["cfg1"] = {"skipped": "config 1 is a one-GPU configuration"}
     if "2" in which:
         if world == 1:
             sub("cfg2", bench_cfg2, cpu_cfg2)

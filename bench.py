@@ -73,6 +73,9 @@ def parse():
                     help="page format of the target cache (tensor-core order or plain rows)")
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                     help="multi-GPU output all-gather: kernel (b)'s own NVLink stores, or NCCL")
+    ap.add_argument("--sub-layers", type=int, default=0,
+                    help="layers of configs 4 and 5 (0 = their own: 36 and 24); smaller cases "
+                         "for profiling")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -827,8 +830,8 @@ class Cfg4:
         c, dev = CFG4, ctx.dev
         self.ctx = ctx
         self.L, self.B, self.T, self.Hq, self.Hk, self.D, self.V = (
-            c["layers"], c["branches"], c["block"], c["qo_heads"], c["kv_heads"], c["head_dim"],
-            c["vocab"])
+            ctx.a.sub_layers or c["layers"], c["branches"], c["block"], c["qo_heads"],
+            c["kv_heads"], c["head_dim"], c["vocab"])
         L, B, T, Hq, Hk, D, V = self.L, self.B, self.T, self.Hq, self.Hk, self.D, self.V
         lens = cfg4_lengths()
         self.total_requests = len(lens)
@@ -1071,7 +1074,8 @@ class Cfg5:
         import d2sd_b200 as d
         c, dev, world, rank = CFG5, ctx.dev, ctx.world, ctx.rank
         self.ctx = ctx
-        self.L, self.P, self.B, self.T = c["layers"], c["prefix"], c["branches"], c["block"]
+        self.L, self.P, self.B, self.T = (ctx.a.sub_layers or c["layers"], c["prefix"],
+                                          c["branches"], c["block"])
         L, P, B, T, D, V, W = self.L, self.P, self.B, self.T, c["head_dim"], c["vocab"], c["window"]
         self.D, self.V, self.W = D, V, W
         if c["kv_heads"] % world:

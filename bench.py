@@ -77,6 +77,9 @@ def parse():
                     help="layers of configs 4 and 5 (0 = their own: 36 and 24); smaller cases "
                          "for profiling")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--flashinfer", action="store_true",
+                    help="config 3, one GPU: also time the reference's own GPU path (FlashInfer "
+                         "kernels, JIT-compiled on first use) on the same inputs and compare")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -752,6 +755,8 @@ def bench_cfg3(ctx: Ctx) -> dict:
                                 "max_us": ctx.max(xwait["max_wait_us"]), "waits": xwait["waits"]}
     if not a.no_e2e:
         out["e2e"] = e2e_cfg3(ctx, c)
+    if a.flashinfer and ctx.world == 1:
+        out["flashinfer"] = flashinfer_cfg3(ctx, c, ab_b2b)
     ctx.barrier()  # no kernel of any rank is still using the peer buffers
     c.close()
     ctx.barrier()  # every rank has unmapped its peers' buffers before they are freed
@@ -812,6 +817,113 @@ def e2e_cfg3(ctx: Ctx, c: Cfg3) -> dict:
     check_status(ctx, "config 3 end to end", c.statuses())
     return {"value": N * a.steps / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": e_ms / a.steps}
+
+
+def flashinfer_cfg3(ctx: Ctx, c: Cfg3, ab_ms: float) -> dict:
+    """The reference's own GPU path of one config-3 layer on the same inputs,
+    as generation/verification.py:139-165 and model/cascade_graph.py:37-112
+    run it: the DynamicCache [Hk, P, D] prefix transposed to NHD, FlashInfer's
+    single_prefill_with_kv_cache over it (level 1), then the runner's copies
+    in, B x (causal single_prefill + merge_state_in_place) and copies out.
+    Everything is captured in one CUDA graph (the reference runs level 1
+    eagerly: this favours it). Also a second parity reference: FlashInfer's
+    merged output against kernels (a)+(b) on the same layer."""
+    import torch
+    try:
+        import flashinfer
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer import failed: {type(e).__name__}: {e}"}
+    B, T, N, hq, hk, D, P = c.B, c.T, c.N, c.hq, c.hk, c.D, c.P
+    if c.ctx.a.shared:
+        return {"unavailable": "the reference path has no shared-trunk form"}
+    k_tok, v_tok = c.cache.gather(0, P)
+    k_hnd, v_hnd = k_tok.transpose(0, 1).contiguous(), v_tok.transpose(0, 1).contiguous()
+    del k_tok, v_tok
+    q_all = c.q_full[0]                      # [B*T, Hq, D]
+    q_fi = q_all.view(B, T, hq, D)
+    kn, vn = c.kn[0], c.vn[0]                # [B, T, Hk, D]
+    k_new = kn.transpose(1, 2)               # the projections' [B, Hk, T, D] view
+    v_new = vn.transpose(1, 2)
+    bufs = {n: torch.empty_like(t) for n, t in (("q", q_fi), ("k", kn), ("v", vn))}
+    bufs["out"] = torch.empty(B, T, hq, D, dtype=torch.bfloat16, device=ctx.dev)
+    bufs["lse"] = torch.empty(B, T, hq, dtype=torch.float32, device=ctx.dev)
+    res = {}
+
+    def level1():
+        kf = k_hnd.transpose(0, 1).contiguous()
+        vf = v_hnd.transpose(0, 1).contiguous()
+        o, s = flashinfer.single_prefill_with_kv_cache(q_all, kf, vf, causal=False,
+                                                       return_lse=True, sm_scale=c.scale)
+        res["o"], res["s"] = o.view(B, T, hq, D), s.view(B, T, hq)
+
+    def local_merge():
+        for i in range(B):
+            ol, sl = flashinfer.single_prefill_with_kv_cache(
+                bufs["q"][i], bufs["k"][i], bufs["v"][i], causal=True, return_lse=True,
+                sm_scale=c.scale)
+            flashinfer.merge_state_in_place(bufs["out"][i], bufs["lse"][i], ol, sl)
+
+    def layer():
+        level1()
+        k_fi, v_fi = k_new.transpose(1, 2).contiguous(), v_new.transpose(1, 2).contiguous()
+        bufs["q"].copy_(q_fi)
+        bufs["k"].copy_(k_fi)
+        bufs["v"].copy_(v_fi)
+        bufs["out"].copy_(res["o"])
+        bufs["lse"].copy_(res["s"])
+        local_merge()
+        res["o"].copy_(bufs["out"])
+        res["s"].copy_(bufs["lse"])
+
+    def prefill_only():
+        flashinfer.single_prefill_with_kv_cache(q_all, k_tok_nhd, v_tok_nhd, causal=False,
+                                                return_lse=True, sm_scale=c.scale)
+
+    try:
+        t0 = time.perf_counter()
+        for _ in range(3):  # JIT compile + warm-up, eagerly
+            layer()
+        torch.cuda.synchronize()
+        compile_s = time.perf_counter() - t0
+        k_tok_nhd, v_tok_nhd = k_hnd.transpose(0, 1).contiguous(), v_hnd.transpose(0, 1).contiguous()
+        prefill_only()
+        torch.cuda.synchronize()
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"flashinfer failed: {type(e).__name__}: {str(e)[:300]}"}
+    layer_ms = graph_ms(ctx, lambda i: layer(), 8)
+    prefill_ms = graph_ms(ctx, lambda i: prefill_only(), 8)
+    transpose_ms = graph_ms(ctx, lambda i: (k_hnd.transpose(0, 1).contiguous(),
+                                           v_hnd.transpose(0, 1).contiguous()), 8)
+    # parity: FlashInfer's merged layer-0 output against kernels (a)+(b)
+    layer()
+    c.run_ab(0)
+    torch.cuda.synchronize()
+    ours_o, ours_s = c.out.float().view(B, T, hq, D), c.lse.view(B, T, hq)
+    fo, fs = res["o"].float(), res["s"]
+    err = (ours_o - fo).abs()
+    within = (err <= 2e-2 + 1e-2 * fo.abs()).float().mean().item()
+    flops = 4.0 * N * hq * P * D
+    hbm, tf_burst, _, _ = measured_peaks()
+    out = {
+        "what": ("the reference's GPU path of one layer (verification.py:139-165 with the "
+                 "CascadeGraphRunner): prefix transpose copy, FlashInfer single_prefill (level 1), "
+                 "runner copies, 8 x (causal single_prefill + merge_state_in_place); one CUDA graph"),
+        "flashinfer_version": getattr(flashinfer, "__version__", "?"),
+        "jit_and_warmup_s": compile_s,
+        "layer_us": layer_ms * 1e3,
+        "single_prefill_us": prefill_ms * 1e3,
+        "single_prefill_tflops": flops / (prefill_ms / 1e3) / 1e12,
+        "single_prefill_frac_of_burst_bf16": flops / (prefill_ms / 1e3) / 1e12 / tf_burst,
+        "transpose_copy_us": transpose_ms * 1e3,
+        "d2sd_ab_us": ab_ms * 1e3,
+        "layer_speedup": layer_ms / ab_ms,
+        "parity_vs_d2sd": {"max_abs_out": err.max().item(),
+                           "max_abs_lse": (ours_s - fs).abs().max().item(),
+                           "frac_within_2e-2_abs_1e-2_rel": within},
+    }
+    del k_hnd, v_hnd, k_tok_nhd, v_tok_nhd, bufs, res
+    torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------

@@ -244,12 +244,6 @@ struct AcceptExchange {
 
 constexpr int A_ARRIVE0 = 0;  // + epoch parity (control block words)
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kThreads)
     accept_kernel(const T* __restrict__ logits, Shape sh, const int64_t* __restrict__ ids,
@@ -296,13 +290,11 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
     u = re;
   }
-  if (threadIdx.x == 0) {
-    __threadfence();
-    last = atomicAdd(ws.ticket, 1u) == gridDim.x - 1;
-  }
+  // one GPU-scope acq_rel ticket per CTA publishes its segment records; the
+  // last CTA's thread 0 acquires them all and the barrier hands them on
+  if (threadIdx.x == 0) last = atom_add_acq_rel_gpu(ws.ticket, 1u) == gridDim.x - 1;
   __syncthreads();
   if (!last) return;
-  __threadfence();
 
   // ---- last CTA: stage the block ids, then per-row argmax over the (at most
   // a few) CTA segments of the row ----
@@ -370,13 +362,13 @@ __global__ void __launch_bounds__(kThreads)
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence_system();
+      fence_acq_rel_sys();  // the one system-scope fence of the launch
       const int par = static_cast<int>(ax.epoch & 1);
-      for (int d = 0; d < ax.world; ++d) atomicAdd_system(ax.ctl[d] + A_ARRIVE0 + par, 1ull);
+      for (int d = 0; d < ax.world; ++d) red_add_relaxed_sys(ax.ctl[d] + A_ARRIVE0 + par, 1ull);
       unsigned long long* mine = ax.ctl[ax.rank] + A_ARRIVE0 + par;
       const uint64_t t0 = global_timer_ns();
       int ok = 1;
-      while (ld_acquire_sys_u64(mine) < static_cast<unsigned long long>(ax.world)) {
+      while (ld_acquire_sys(mine) < static_cast<unsigned long long>(ax.world)) {
         if (global_timer_ns() - t0 > kWaitTimeoutNs) {
           ok = 0;
           break;
@@ -386,8 +378,7 @@ __global__ void __launch_bounds__(kThreads)
       else atomicExch(ax.status, 3);
       s_ok = ok;
     }
-    __syncthreads();
-    __threadfence_system();
+    __syncthreads();  // thread 0's acquire of the peers' records, handed on to the CTA
     const uint4* in = reinterpret_cast<const uint4*>(ax.rec[(ax.epoch & 1) * ax.world + ax.rank]);
     for (int r = threadIdx.x; r < rows; r += kThreads) {
       float bv = -INFINITY;

@@ -143,6 +143,37 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// Hand-offs between the CTAs of a grid and between GPUs. Every CTA publishes
+// its results with ONE acq_rel atomic at GPU scope on a ticket (its threads'
+// stores are ordered before it by the CTA barrier that precedes it); the CTA
+// that draws the last ticket has thereby acquired every other CTA's stores,
+// and a single system-scope fence by that one thread then orders all of them
+// -- NVLink stores into peer memory included, since release/acquire chains are
+// cumulative in the PTX memory model -- before the relaxed system-scope signal
+// the peers acquire. System-scope fences are expensive and do not overlap
+// across CTAs (one per CTA cost about 10 us per launch at 256 CTAs), so each
+// launch issues exactly one.
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ unsigned long long atom_add_acq_rel_gpu(unsigned long long* p,
+                                                                   unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -324,9 +355,10 @@ __device__ __forceinline__ uint64_t umma_desc_noswz(uint32_t smem_addr, uint32_t
 // serialisation may start while the previous kernel of its stream still runs;
 // grid_dep_wait() returns once that kernel has completed and its memory is
 // visible (at once for a normal launch). grid_dep_launch() lets the next
-// kernel of the stream start early; kernels here issue it only after their own
-// grid_dep_wait(), so whatever they hand on is ordered after everything that
-// preceded them.
+// kernel of the stream start early. The next kernel's grid_dep_wait() still
+// waits for the whole of this kernel, so ordering holds whether a kernel
+// issues grid_dep_launch() before its own grid_dep_wait() (kernel (b): its
+// level-2 half needs nothing from its predecessor) or after it (kernel (a)).
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

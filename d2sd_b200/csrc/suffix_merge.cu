@@ -85,12 +85,6 @@ constexpr int X_WAIT_NS = 3;   // total time the signalling CTA waited for the p
 constexpr int X_WAITS = 4;     // number of completed waits
 constexpr int X_WAIT_MAX = 5;  // longest wait
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 template <typename T>
 struct Fmt;
 template <>
@@ -558,9 +552,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   if (p.world > 0) {
-    // Arrival. Every CTA makes its peer stores visible system-wide and takes a
-    // ticket; the CTA that takes the last one signals every rank once (one
-    // NVLink atomic per peer per call instead of one per CTA) and then waits,
+    // Arrival. Every CTA publishes its rows (local and NVLink stores) with one
+    // GPU-scope acq_rel ticket; the CTA that draws the last ticket has acquired
+    // all of them, issues the launch's single system-scope fence and signals
+    // every rank once (one NVLink atomic per peer per call), then waits,
     // bounded, until every rank has signalled this rank, so that the kernel
     // completes only when this rank's buffer is whole.
     // The arrival counters alternate with the epoch parity and the waiting CTA
@@ -570,14 +565,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // count to wait for is world, whatever the grid of this call or the last.
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence_system();
       unsigned long long* mine = p.peer_ctr[p.rank];
       const unsigned long long ctas =
           static_cast<unsigned long long>(gridDim.x) * gridDim.y * gridDim.z;
-      if (atomicAdd(mine + X_TICKET, 1ull) == ctas - 1) {
-        __threadfence_system();
+      if (atom_add_acq_rel_gpu(mine + X_TICKET, 1ull) == ctas - 1) {
+        fence_acq_rel_sys();
         const int par = static_cast<int>(p.epoch & 1);
-        for (int d = 0; d < p.world; ++d) atomicAdd_system(p.peer_ctr[d] + X_ARRIVE0 + par, 1ull);
+        for (int d = 0; d < p.world; ++d) red_add_relaxed_sys(p.peer_ctr[d] + X_ARRIVE0 + par, 1ull);
         const uint64_t t0 = global_timer_ns();
         bool ok = true;
         while (ld_acquire_sys(mine + X_ARRIVE0 + par) < static_cast<unsigned long long>(p.world)) {
@@ -598,7 +592,6 @@ __global__ void __launch_bounds__(kThreads, 2)
           atomicExch(p.status, 3);
         }
         atomicExch(mine + X_TICKET, 0ull);
-        __threadfence_system();
       }
     }
   }

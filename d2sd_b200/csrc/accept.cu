@@ -8,8 +8,9 @@
 //         stop if no branch is valid
 // The argmax is a pure function of one logits row, so every row's argmax is
 // computed up front (that is the whole cost: B*T*V logits read once, coalesced
-// 16-byte loads, HBM-bound) and the walk then runs on one warp with a ballot
-// per step. The winning branch returned is vb of the last iteration, the branch
+// 16-byte loads, HBM-bound); the walk then needs, per step, only whether each
+// branch's next draft equals the emitted token, which is precomputed per row as
+// a bit mask over the branches. The winning branch returned is vb of the last iteration, the branch
 // whose logits produced the bonus token and whose K/V the commit appends
 // (generation/d3_generator.py:229-230).
 // Ties resolve to the first maximal index and NaN counts as maximal (first NaN
@@ -18,8 +19,9 @@
 // Work: the 16-byte vectors of all logits rows, flattened, are split evenly
 // over the grid (stream-K: a CTA's range may cross rows); each thread keeps 8
 // loads in flight and each CTA records one (max, first index) per row segment.
-// The CTA that finishes last (atomic ticket) reduces the segments of every row
-// and runs the walks, one warp per request.
+// The CTA that finishes last (atomic ticket) reduces the segments of every row,
+// forms the rows' match masks (all threads) and runs the walks, one thread per
+// request (a shared-memory load and a find-first-set per step).
 // Modes: one request (d2sd_verify_accept); a batch of requests with their own
 // logits, ids and results in one launch (d2sd_verify_accept_batch, batched
 // serving); and a vocabulary-sharded launch (d2sd_verify_accept_sharded) in
@@ -49,7 +51,6 @@ __device__ __forceinline__ bool better(float va, int64_t ia, float vb, int64_t i
 }
 
 constexpr int kBatch = 8;       // 16-byte loads in flight per thread
-constexpr int kIdsCache = 2048; // block ids staged in shared memory for the walk
 
 // Stream-K partition of the flattened (row, unit) space over the grid: CTA c
 // owns units [c*W, (c+1)*W), W = ceil(total / grid); a unit is one 16-byte
@@ -68,34 +69,44 @@ __host__ __device__ inline Part partition(int64_t rows, int64_t upr, int64_t gri
   return p;
 }
 
-// Rows a CTA's range can touch: ceil(W / upr) + 1 <= ceil(rows / grid) + 2.
-__host__ __device__ inline int64_t max_segments(int64_t rows, int64_t grid) {
-  return (rows + grid - 1) / grid + 2;
+// Segments one row can span: the row's units [r*upr, (r+1)*upr) meet at most
+// ceil((upr - 1) / W) + 1 CTA ranges, and upr / W <= grid / rows, so
+// ceil(grid / rows) + 2 slots per row always suffice (whatever the vector width).
+__host__ __device__ inline int64_t slots_per_row(int64_t rows, int64_t grid) {
+  return (grid + rows - 1) / rows + 2;
 }
 
+// Per-row records of the scan: CTA c writes the (max, first index) of its part
+// of row r into slot c - c_first(r) of the row, and the CTA holding the row's
+// last unit writes the row's slot count; the last CTA reads them by row, with
+// no division.
 struct Workspace {
   unsigned int* ticket;  // CTAs finished; zero between launches
-  float* pval;           // [grid][segs]
-  int64_t* pidx;         // [grid][segs]
-  int64_t segs;
+  float* rval;           // [rows][S]
+  int64_t* ridx;         // [rows][S]
+  int32_t* rcount;       // [rows]
+  int64_t S;
 };
 
 __host__ __device__ inline int64_t align_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 __host__ __device__ inline int64_t workspace_bytes(int64_t rows, int64_t grid) {
-  const int64_t n = grid * max_segments(rows, grid);
-  return 256 + align_up(n * 4, 256) + align_up(n * 8, 256);
+  const int64_t n = rows * slots_per_row(rows, grid);
+  return 256 + align_up(n * 4, 256) + align_up(n * 8, 256) + align_up(rows * 4, 256);
 }
 
 __host__ __device__ inline Workspace carve(void* base, int64_t rows, int64_t grid) {
   uint8_t* b = static_cast<uint8_t*>(base);
   Workspace w;
-  w.segs = max_segments(rows, grid);
+  w.S = slots_per_row(rows, grid);
+  const int64_t n = rows * w.S;
   w.ticket = reinterpret_cast<unsigned int*>(b);
   b += 256;
-  w.pval = reinterpret_cast<float*>(b);
-  b += align_up(grid * w.segs * 4, 256);
-  w.pidx = reinterpret_cast<int64_t*>(b);
+  w.rval = reinterpret_cast<float*>(b);
+  b += align_up(n * 4, 256);
+  w.ridx = reinterpret_cast<int64_t*>(b);
+  b += align_up(n * 8, 256);
+  w.rcount = reinterpret_cast<int32_t*>(b);
   return w;
 }
 
@@ -128,6 +139,18 @@ struct VecMax<float> {
     return max_nan(max_nan(__uint_as_float(v.x), __uint_as_float(v.y)),
                    max_nan(__uint_as_float(v.z), __uint_as_float(v.w)));
   }
+  // maximum of a whole batch of vectors (a tree: short dependency chains)
+  template <int N>
+  static __device__ __forceinline__ float batch(const uint4 (&v)[N]) {
+    float m[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) m[k] = max(v[k]);
+#pragma unroll
+    for (int w = 1; w < N; w *= 2)
+#pragma unroll
+      for (int k = 0; k + w < N; k += 2 * w) m[k] = max_nan(m[k], m[k + w]);
+    return m[0];
+  }
 };
 __device__ __forceinline__ uint32_t max_nan_bf16x2(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -146,12 +169,37 @@ struct VecMax<__nv_bfloat16> {
     // bf16 -> f32 is a shift of the bit pattern
     return max_nan(__uint_as_float(m << 16), __uint_as_float(m & 0xffff0000u));
   }
+  template <int N>
+  static __device__ __forceinline__ float batch(const uint4 (&v)[N]) {
+    uint32_t m[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+      m[k] = max_nan_bf16x2(max_nan_bf16x2(v[k].x, v[k].y), max_nan_bf16x2(v[k].z, v[k].w));
+#pragma unroll
+    for (int w = 1; w < N; w *= 2)
+#pragma unroll
+      for (int k = 0; k + w < N; k += 2 * w) m[k] = max_nan_bf16x2(m[k], m[k + w]);
+    return max_nan(__uint_as_float(m[0] << 16), __uint_as_float(m[0] & 0xffff0000u));
+  }
 };
 template <>
 struct VecMax<__half> {
   static __device__ __forceinline__ float max(const uint4& v) {
     const uint32_t m = max_nan_f16x2(max_nan_f16x2(v.x, v.y), max_nan_f16x2(v.z, v.w));
     const __half2 h = *reinterpret_cast<const __half2*>(&m);
+    return max_nan(__low2float(h), __high2float(h));
+  }
+  template <int N>
+  static __device__ __forceinline__ float batch(const uint4 (&v)[N]) {
+    uint32_t m[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+      m[k] = max_nan_f16x2(max_nan_f16x2(v[k].x, v[k].y), max_nan_f16x2(v[k].z, v[k].w));
+#pragma unroll
+    for (int w = 1; w < N; w *= 2)
+#pragma unroll
+      for (int k = 0; k + w < N; k += 2 * w) m[k] = max_nan_f16x2(m[k], m[k + w]);
+    const __half2 h = *reinterpret_cast<const __half2*>(&m[0]);
     return max_nan(__low2float(h), __high2float(h));
   }
 };
@@ -173,47 +221,80 @@ __device__ __forceinline__ void warp_argmax(float& v, int64_t& i) {
 // only a vector that beats the running best (or holds a NaN) is searched for
 // its first maximal index. A strict ">" keeps the first index among equal
 // maxima; once the best is NaN nothing replaces it (first NaN wins).
+// Whole batches of kBatch vectors take a fast path: the batch's maximum is
+// formed from the vectors' maxima (independent of one another, so the chain
+// is short), and only a batch whose maximum beats the best -- a handful of
+// times per row for any data -- is walked vector by vector with the exact
+// rule above. The ragged end of the range goes through the exact rule directly.
+template <typename T>
+__device__ __forceinline__ void update_vec(const uint4& raw, float vm, int64_t first, float& best_v,
+                                           int64_t& best_i) {
+  if (!(vm <= best_v) && best_v == best_v) {
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int j = 0; j < Vec<T>::N; ++j) {
+      const float x = Num<T>::to_f(e[j]);
+      if (x != x || x == vm) {
+        best_v = x;
+        best_i = first + j;
+        break;
+      }
+    }
+  }
+}
+
 template <typename T, bool VEC>
 __device__ __forceinline__ void scan_units(const T* __restrict__ row, int64_t u0, int64_t u1,
                                            int stride, float& best_v, int64_t& best_i) {
   constexpr int VN = VEC ? Vec<T>::N : 1;
-  for (int64_t u = u0; u < u1; u += static_cast<int64_t>(stride) * kBatch) {
-    if (VEC) {
+  if (u0 < u1 && best_i == INT64_MAX) best_i = u0 * VN;  // first element seen
+  int64_t u = u0;
+  if (VEC) {
+    const uint4* base = reinterpret_cast<const uint4*>(row);
+    const int64_t span = static_cast<int64_t>(stride) * kBatch;
+    for (; u + static_cast<int64_t>(stride) * (kBatch - 1) < u1; u += span) {
+      const uint4* p = base + u;
+      uint4 raw[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) raw[k] = __ldg(p + k * stride);
+      const float m = VecMax<T>::batch(raw);
+      if (!(m <= best_v) && best_v == best_v) {
+        // the batch beats the best: its first element equal to m (first NaN
+        // if m is NaN) is the new best -- in the first vector whose maximum is m
+        int kk = 0;
+#pragma unroll
+        for (int k = kBatch - 1; k >= 0; --k) {
+          const float vk = VecMax<T>::max(raw[k]);
+          if (vk == m || (m != m && vk != vk)) kk = k;
+        }
+        uint4 sel = raw[0];
+#pragma unroll
+        for (int k = 1; k < kBatch; ++k)
+          if (k == kk) sel = raw[k];
+        update_vec<T>(sel, m, (u + static_cast<int64_t>(kk) * stride) * VN, best_v, best_i);
+      }
+    }
+    if (u < u1) {  // the ragged end: fewer than kBatch vectors left
       uint4 raw[kBatch];
 #pragma unroll
       for (int k = 0; k < kBatch; ++k) {
         const int64_t uu = u + static_cast<int64_t>(k) * stride;
-        if (uu < u1) raw[k] = __ldg(reinterpret_cast<const uint4*>(row) + uu);
+        if (uu < u1) raw[k] = __ldg(base + uu);
       }
 #pragma unroll
       for (int k = 0; k < kBatch; ++k) {
         const int64_t uu = u + static_cast<int64_t>(k) * stride;
-        if (uu >= u1) break;
-        if (best_i == INT64_MAX) best_i = uu * VN;  // first element seen
-        const float vm = VecMax<T>::max(raw[k]);
-        if (!(vm <= best_v) && best_v == best_v) {
-          const T* e = reinterpret_cast<const T*>(&raw[k]);
-#pragma unroll
-          for (int j = 0; j < Vec<T>::N; ++j) {
-            const float x = Num<T>::to_f(e[j]);
-            if (x != x || x == vm) {
-              best_v = x;
-              best_i = uu * VN + j;
-              break;
-            }
-          }
-        }
+        if (uu < u1) update_vec<T>(raw[k], VecMax<T>::max(raw[k]), uu * VN, best_v, best_i);
       }
-    } else {
+    }
+  } else {
+    for (; u < u1; u += static_cast<int64_t>(stride) * kBatch) {
 #pragma unroll 1
       for (int k = 0; k < kBatch; ++k) {
         const int64_t uu = u + static_cast<int64_t>(k) * stride;
         if (uu >= u1) break;
         const float x = Num<T>::to_f(row[uu]);
-        if (best_i == INT64_MAX) {
-          best_v = x;
-          best_i = uu;
-        } else if ((x > best_v || (x != x)) && best_v == best_v) {
+        if ((x > best_v || (x != x)) && best_v == best_v) {
           best_v = x;
           best_i = uu;
         }
@@ -245,23 +326,23 @@ struct AcceptExchange {
 constexpr int A_ARRIVE0 = 0;  // + epoch parity (control block words)
 
 template <typename T, bool VEC>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)  // the grid is 3 CTAs per SM
     accept_kernel(const T* __restrict__ logits, Shape sh, const int64_t* __restrict__ ids,
                   int32_t* result, int64_t* accepted, int64_t* argmax_out, Workspace ws, Part pt,
                   AcceptExchange ax) {
   __shared__ float sv[kThreads / 32];
   __shared__ int64_t si[kThreads / 32];
   __shared__ bool last;
-  __shared__ int32_t s_amax[64 * 64];
-  __shared__ int64_t s_ids[kIdsCache];
+  // last CTA only (dynamic, rows * 16 bytes): per row its match mask, its
+  // argmax and its draft id
+  extern __shared__ __align__(16) uint8_t s_dyn[];
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int TB = sh.TB, B = sh.B;
   const int bt = B * TB;
   const int rows = sh.R * bt;
   const int64_t u_begin = static_cast<int64_t>(blockIdx.x) * pt.W;
   const int64_t u_end = u_begin + pt.W < pt.total ? u_begin + pt.W : pt.total;
-  int seg = 0;
-  for (int64_t u = u_begin; u < u_end; ++seg) {
+  for (int64_t u = u_begin; u < u_end;) {
     const int64_t r = u / pt.upr;
     const int64_t re = (r + 1) * pt.upr < u_end ? (r + 1) * pt.upr : u_end;
     const int q = static_cast<int>(r / bt);
@@ -284,8 +365,11 @@ __global__ void __launch_bounds__(kThreads)
           bi = si[w];
         }
       }
-      ws.pval[blockIdx.x * ws.segs + seg] = bv;
-      ws.pidx[blockIdx.x * ws.segs + seg] = bi;
+      // this CTA's slot in the row: its index minus that of the row's first CTA
+      const int64_t k = blockIdx.x - (r * pt.upr) / pt.W;
+      ws.rval[r * ws.S + k] = bv;
+      ws.ridx[r * ws.S + k] = bi;
+      if (re == (r + 1) * pt.upr) ws.rcount[r] = static_cast<int32_t>(k + 1);  // the row ends here
     }
     __syncthreads();
     u = re;
@@ -296,63 +380,79 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (!last) return;
 
-  // ---- last CTA: stage the block ids, then per-row argmax over the (at most
-  // a few) CTA segments of the row ----
-  const bool ids_cached = rows <= kIdsCache;
-  auto id_at = [&](int q, int b, int t) -> int64_t {
-    return ids[q * sh.i_r + b * sh.i_b + t * sh.i_t];
-  };
-  if (ids_cached) {
-    for (int r = threadIdx.x; r < rows; r += kThreads)
-      s_ids[r] = id_at(r / bt, (r / TB) % B, r % TB);
-  }
-  for (int r = threadIdx.x; r < rows; r += kThreads) {
-    const int64_t c_first = (static_cast<int64_t>(r) * pt.upr) / pt.W;
-    const int64_t c_last = ((static_cast<int64_t>(r) + 1) * pt.upr - 1) / pt.W;
-    float v[4];
-    int64_t ix[4];
+  // ---- last CTA: per-row argmax over the (at most a few) CTA segments of the
+  // row and the rows' draft ids into shared memory, then the match masks, then
+  // the walks. Each thread keeps the loads of kRowsInFlight rows in flight
+  // together (rows do not depend on one another), so the phase costs a couple
+  // of round trips to L2 however many rows a thread owns. ----
+  uint64_t* s_mask = reinterpret_cast<uint64_t*>(s_dyn);
+  int32_t* s_amax = reinterpret_cast<int32_t*>(s_dyn + static_cast<size_t>(rows) * 8);
+  int32_t* s_ids = s_amax + rows;
+  // (rows that span more than kSlotsInFlight CTAs exist only when rows are
+  // fewer than CTAs, i.e. at most one row per thread)
+  constexpr int kRowsInFlight = 4, kSlotsInFlight = 2;
+  for (int rb = threadIdx.x; rb < rows; rb += kRowsInFlight * kThreads) {
+    float v[kRowsInFlight][kSlotsInFlight];
+    int64_t ix[kRowsInFlight][kSlotsInFlight];
+    int64_t idv[kRowsInFlight];
+    int cnt[kRowsInFlight];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {  // the common case: up to 4 segments, loads in flight together
-      const int64_t c = c_first + k;
-      if (c <= c_last) {
-        const int64_t seg = r - (c * pt.W) / pt.upr;  // segment of CTA c holding row r
-        v[k] = __ldcg(ws.pval + c * ws.segs + seg);
-        ix[k] = __ldcg(ws.pidx + c * ws.segs + seg);
-      }
-    }
-    float bv = -INFINITY;
-    int64_t bi = INT64_MAX;
+    for (int j = 0; j < kRowsInFlight; ++j) {
+      const int r = rb + j * kThreads;
+      if (r < rows) {
+        const int q = r / bt, b = (r / TB) % B, t = r % TB;
+        idv[j] = __ldg(ids + q * sh.i_r + b * sh.i_b + t * sh.i_t);
+        cnt[j] = __ldcg(ws.rcount + r);
+        // the first slots of the row, loaded before the count is known (slots
+        // past the count hold stale values and are ignored)
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (c_first + k <= c_last && better(v[k], ix[k], bv, bi)) {
-        bv = v[k];
-        bi = ix[k];
+        for (int k = 0; k < kSlotsInFlight; ++k) {
+          if (k < ws.S) {
+            v[j][k] = __ldcg(ws.rval + r * ws.S + k);
+            ix[j][k] = __ldcg(ws.ridx + r * ws.S + k);
+          }
+        }
       }
     }
-    for (int64_t c = c_first + 4; c <= c_last; ++c) {
-      const int64_t seg = r - (c * pt.W) / pt.upr;
-      const float vv = __ldcg(ws.pval + c * ws.segs + seg);
-      const int64_t ii = __ldcg(ws.pidx + c * ws.segs + seg);
-      if (better(vv, ii, bv, bi)) {
-        bv = vv;
-        bi = ii;
+#pragma unroll
+    for (int j = 0; j < kRowsInFlight; ++j) {
+      const int r = rb + j * kThreads;
+      if (r >= rows) break;
+      // a draft id no argmax can equal (negative, or beyond 31 bits) becomes -1
+      s_ids[r] = (idv[j] >= 0 && idv[j] <= INT32_MAX) ? static_cast<int32_t>(idv[j]) : -1;
+      float bv = -INFINITY;
+      int64_t bi = INT64_MAX;
+#pragma unroll
+      for (int k = 0; k < kSlotsInFlight; ++k) {
+        if (k < cnt[j] && better(v[j][k], ix[j][k], bv, bi)) {
+          bv = v[j][k];
+          bi = ix[j][k];
+        }
       }
-    }
-    if (bi == INT64_MAX) bi = 0;
-    bi += sh.vocab_offset;
-    if (ax.world > 0) {
-      // the row's best of this vocabulary slice into every rank's buffer
-      uint4 rec;
-      rec.x = __float_as_uint(bv);
-      rec.y = 0u;
-      rec.z = static_cast<uint32_t>(static_cast<uint64_t>(bi));
-      rec.w = static_cast<uint32_t>(static_cast<uint64_t>(bi) >> 32);
-      void* const* outs = ax.rec + (ax.epoch & 1) * ax.world;
-      for (int d = 0; d < ax.world; ++d)
-        reinterpret_cast<uint4*>(outs[d])[static_cast<int64_t>(ax.rank) * rows + r] = rec;
-    } else {
-      s_amax[r] = static_cast<int32_t>(bi);
-      if (argmax_out) argmax_out[r] = bi;
+      for (int k = kSlotsInFlight; k < cnt[j]; ++k) {  // rows over more CTAs
+        const float vv = __ldcg(ws.rval + r * ws.S + k);
+        const int64_t ii = __ldcg(ws.ridx + r * ws.S + k);
+        if (better(vv, ii, bv, bi)) {
+          bv = vv;
+          bi = ii;
+        }
+      }
+      if (bi == INT64_MAX) bi = 0;
+      bi += sh.vocab_offset;
+      if (ax.world > 0) {
+        // the row's best of this vocabulary slice into every rank's buffer
+        uint4 rec;
+        rec.x = __float_as_uint(bv);
+        rec.y = 0u;
+        rec.z = static_cast<uint32_t>(static_cast<uint64_t>(bi));
+        rec.w = static_cast<uint32_t>(static_cast<uint64_t>(bi) >> 32);
+        void* const* outs = ax.rec + (ax.epoch & 1) * ax.world;
+        for (int d = 0; d < ax.world; ++d)
+          reinterpret_cast<uint4*>(outs[d])[static_cast<int64_t>(ax.rank) * rows + r] = rec;
+      } else {
+        s_amax[r] = static_cast<int32_t>(bi);
+        if (argmax_out) argmax_out[r] = bi;
+      }
     }
   }
   if (ax.world > 0) {
@@ -399,8 +499,24 @@ __global__ void __launch_bounds__(kThreads)
   }
   __syncthreads();
 
-  // ---- the acceptance walks, one warp per request (valid set as a 64-bit mask) ----
-  for (int q = warp; q < sh.R; q += kThreads / 32) {
+  // ---- match masks: row r = (request q, branch b', position t) with argmax
+  // tok gets bit b for every branch b whose draft at position t + 1 is tok --
+  // the test the walk makes after emitting tok from branch b' at position t ----
+  for (int r = threadIdx.x; r < rows; r += kThreads) {
+    const int q = r / bt, t = r % TB;
+    const int32_t tok = s_amax[r];
+    uint64_t m = 0;
+    if (t + 1 < TB) {
+      const int32_t* id_next = s_ids + q * bt + t + 1;
+      for (int b = 0; b < B; ++b) m |= static_cast<uint64_t>(id_next[b * TB] == tok) << b;
+    }
+    s_mask[r] = m;
+  }
+  __syncthreads();
+
+  // ---- the acceptance walks, one thread per request: the valid branches as a
+  // 64-bit mask, one shared-memory mask per step ----
+  for (int q = threadIdx.x; q < sh.R; q += kThreads) {
     const int r0 = q * bt;
     uint64_t valid = (B >= 64) ? ~0ull : ((1ull << B) - 1ull);
     int acc = 0;
@@ -408,24 +524,16 @@ __global__ void __launch_bounds__(kThreads)
     int64_t* acc_q = accepted + static_cast<int64_t>(q) * TB;
     while (true) {
       vb = __ffsll(static_cast<long long>(valid)) - 1;
-      const int64_t tok = s_amax[r0 + vb * TB + acc];
-      if (lane == 0) acc_q[acc] = tok;
+      const int r = r0 + vb * TB + acc;
+      acc_q[acc] = s_amax[r];
       acc += 1;
       if (acc == TB) break;
-      bool m0 = false, m1 = false;
-      if (lane < B) m0 = (ids_cached ? s_ids[r0 + lane * TB + acc] : id_at(q, lane, acc)) == tok;
-      if (lane + 32 < B)
-        m1 = (ids_cached ? s_ids[r0 + (lane + 32) * TB + acc] : id_at(q, lane + 32, acc)) == tok;
-      const uint64_t match = static_cast<uint64_t>(__ballot_sync(0xffffffffu, m0)) |
-                             (static_cast<uint64_t>(__ballot_sync(0xffffffffu, m1)) << 32);
-      valid &= match;
+      valid &= s_mask[r];
       if (valid == 0) break;
     }
-    for (int k = acc + lane; k < TB; k += 32) acc_q[k] = -1;
-    if (lane == 0) {
-      result[2 * q] = acc;
-      result[2 * q + 1] = vb;
-    }
+    for (int k = acc; k < TB; ++k) acc_q[k] = -1;
+    result[2 * q] = acc;
+    result[2 * q + 1] = vb;
   }
   if (threadIdx.x == 0) *ws.ticket = 0u;  // leave the workspace zeroed for the next launch
 }
@@ -453,11 +561,29 @@ int launch_accept(const void* logits, const Shape& sh, const int64_t* ids, int32
                    sh.s_r % VN == 0 && sh.s_b % VN == 0 && sh.s_t % VN == 0;
   const int64_t upr = vec ? sh.V / VN : sh.V;
   Part pt = partition(rows, upr, grid);
+  // masks, argmaxes and draft ids of the last CTA
+  const size_t smem = static_cast<size_t>(rows) * 16;
+  // up to 64 KiB of dynamic shared memory (4096 rows) on top of the static part
+  // needs the opt-in, once per device and instantiation
+  static int configured[2] = {-1, -1};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured[vec] != dev) {
+    cudaError_t e = vec ? cudaFuncSetAttribute(accept_kernel<T, true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               64 * 64 * 16)
+                        : cudaFuncSetAttribute(accept_kernel<T, false>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               64 * 64 * 16);
+    if (e != cudaSuccess)
+      return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured[vec] = dev;
+  }
   if (vec)
-    accept_kernel<T, true><<<grid, kThreads, 0, stream>>>(static_cast<const T*>(logits), sh, ids,
+    accept_kernel<T, true><<<grid, kThreads, smem, stream>>>(static_cast<const T*>(logits), sh, ids,
                                                           result, acc_ids, argmax_out, ws, pt, ax);
   else
-    accept_kernel<T, false><<<grid, kThreads, 0, stream>>>(static_cast<const T*>(logits), sh, ids,
+    accept_kernel<T, false><<<grid, kThreads, smem, stream>>>(static_cast<const T*>(logits), sh, ids,
                                                            result, acc_ids, argmax_out, ws, pt, ax);
   return check_launch("accept_kernel");
 }

@@ -765,6 +765,42 @@ def bench_cfg3(ctx: Ctx) -> dict:
     return out
 
 
+def bench_cfg3_trunk(ctx: Ctx, shared: int) -> dict:
+    """Config 3 with a tree whose branches share their first `shared` tokens
+    (N_u = k + B*(T-k) unique query rows in kernel (a)): the step timed as the
+    headline's, and kernel (a)'s roofline on the unique rows."""
+    import copy
+
+    import torch
+    a2 = copy.copy(ctx.a)
+    a2.shared = shared
+    ctx2 = copy.copy(ctx)
+    ctx2.a = a2
+    c = Cfg3(ctx2)
+    ms_total, clocks, graph = timed_steps(ctx2, c.step, a2.steps, a2.warmup)
+    del graph
+    k = kernel_ms(ctx2, c)
+    statuses = check_status(ctx2, f"config 3, trunk {shared}", c.statuses())
+    _, tf_burst, _, peak_src = measured_peaks()
+    flops = 4.0 * c.n_u * c.hq * c.P * c.D
+    achieved = flops / (k["a"] / 1e3) / 1e12
+    out = {"metric": "verified tokens/s", "unit": "tokens/s",
+           "value": c.N * a2.steps / (ms_total / 1e3), "ms_per_step": ms_total / a2.steps,
+           "shared_trunk": shared, "unique_query_tokens": c.n_u, "status": statuses,
+           "clocks": clocks,
+           "roofline": {"bound": "tensor", "kernel": "prefix_attention_kernel (a)",
+                        "achieved": achieved, "peak": tf_burst, "unit": "TFLOP/s",
+                        "frac": achieved / tf_burst, "peak_source": f"bf16_tflops of {peak_src}",
+                        "algorithmic": f"4*N_u*Hq*P*D = {flops:.4g} FLOP per launch"},
+           "kernels": {"a_prefix_attention_us": k["a"] * 1e3, "b_marginal_us": k["b_marginal"] * 1e3,
+                       "c_accept_us": k["c"] * 1e3, "d_commit_us": k["d"] * 1e3},
+           "gpu_launches": a2.steps * (2 * c.L + 2)}
+    c.close()
+    del c
+    torch.cuda.empty_cache()
+    return out
+
+
 def e2e_cfg3(ctx: Ctx, c: Cfg3) -> dict:
     """The same step through the public API from pinned host buffers: each
     step copies every layer's q/k/v (this rank's heads) and the logits (this
@@ -1592,12 +1628,15 @@ def run_d2sd(ctx: Ctx):
                 return
         else:
             subs[name] = fn(ctx)
-        if cpu:
+        if cpu and cpu_fn is not None:
             cb = cpu_fn()
             cb.pop("seconds_per_step", None)
             subs[name]["cpu_baseline"] = cb
 
     head = bench_cfg3(ctx) if "3" in which else None
+    if "3" in which and world == 1 and not a.shared:
+        for k in (4, 8):  # config 3's tree-trunk sweep
+            sub(f"cfg3_trunk{k}", lambda cx, k=k: bench_cfg3_trunk(cx, k), None)
     if "4" in which:
         sub("cfg4", bench_cfg4, cpu_cfg4)
     if "5" in which:

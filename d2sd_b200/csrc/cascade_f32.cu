@@ -12,9 +12,14 @@
 // (generation/verification.py:173-176), in fp32 with exact expf/logf. The LSE
 // it returns is base 2 (FlashInfer's convention, as everywhere in this library).
 //
-// One warp per (token, query head) row, lane l holding dims l, l+32, ...; an
-// online softmax over the keys. The work is small (config 1: 64 rows x 32
-// heads x 528 keys), so plain coalesced loads serve.
+// A CTA takes 16 query rows of one kv head (row = token * G + g, the G query
+// heads of the kv head) and walks the keys in tiles of 32: the prefix keys
+// [kv_start, P), then the block tokens of the blocks its rows' tokens lie in.
+// Each tile's K and V rows are staged in shared memory by 16-byte cp.async
+// copies, one tile ahead of the one being computed. Per tile, a warp (4 rows)
+// computes the 4 x 32 scores with lane = key (Q broadcast from shared memory),
+// updates each row's online softmax (max and sum across the warp), and adds
+// P.V with lane = 4 dims (P broadcast by shuffle). All in fp32 with expf.
 #include "common.cuh"
 
 namespace d2sd {
@@ -46,82 +51,265 @@ struct F32Params {
   float scale;
 };
 
-template <int DW>  // dims per lane: D / 32
-__global__ void __launch_bounds__(128) cascade_f32_kernel(const F32Params p) {
+constexpr int kF32Rows = 16;     // query rows per CTA (4 per warp)
+constexpr int kF32Keys = 32;     // keys per tile (one per lane in Q.K^T)
+constexpr int kF32Threads = 128;
+
+template <int D>
+struct F32Smem {
+  static constexpr int KS = D + 4;  // K row stride: 16-byte rows, conflict-free float4 reads
+  static constexpr int kQ = kF32Rows * D;
+  static constexpr int kK = kF32Keys * KS;
+  static constexpr int kV = kF32Keys * D;
+  static constexpr int kStage = kK + kV;
+  static constexpr size_t kBytes = sizeof(float) * (kQ + 2 * kStage);
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(kF32Threads) cascade_f32_kernel(const F32Params p, int aligned) {
+  using S = F32Smem<D>;
+  constexpr int DW = D / 32;  // dims per lane in P.V and the output
+  extern __shared__ __align__(16) float sm[];
+  float* Qs = sm;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + warp;
-  if (row >= static_cast<int64_t>(p.num_tokens) * p.Hq) return;
-  const int tok = static_cast<int>(row / p.Hq), hq = static_cast<int>(row % p.Hq);
-  const int hk = hq / p.G;
-  float qv[DW], acc[DW];
-  const float* qr = p.q + static_cast<int64_t>(tok) * p.q_st + static_cast<int64_t>(hq) * p.q_sh;
-#pragma unroll
-  for (int k = 0; k < DW; ++k) {
-    qv[k] = qr[lane + 32 * k] * p.scale;
-    acc[k] = 0.f;
-  }
-  float m = -INFINITY, l = 0.f;
-  auto visit = [&](const float* kr, const float* vr) {
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < DW; ++k) s = fmaf(qv[k], kr[lane + 32 * k], s);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float mn = fmaxf(m, s);
-    const float alpha = (m == -INFINITY) ? 0.f : expf(m - mn);
-    const float pj = expf(s - mn);
-    l = fmaf(l, alpha, pj);
-#pragma unroll
-    for (int k = 0; k < DW; ++k) acc[k] = fmaf(acc[k], alpha, pj * vr[lane + 32 * k]);
-    m = mn;
-  };
-  if (p.kp) {
-    const int64_t hoff = static_cast<int64_t>(hk) * p.p_sh;
-    for (int j = p.kv_start; j < p.P; ++j)
-      visit(p.kp + j * p.p_st + hoff, p.vp + j * p.p_st + hoff);
-  }
-  if (p.kl) {
-    const int TB = p.block_len;
-    const int blk = tok / TB, t = tok - (tok / TB) * TB;
-    uint64_t allowed;
-    if (p.mask_mode == D2SD_MASK_CAUSAL) allowed = (t >= 63) ? ~0ull : ((2ull << t) - 1ull);
-    else if (p.mask_mode == D2SD_MASK_CUSTOM) allowed = p.custom_mask[tok];
-    else allowed = ~0ull;
-    const int64_t hoff = static_cast<int64_t>(hk) * p.l_sh;
-    for (int j = 0; j < TB; ++j) {
-      if (!((allowed >> j) & 1ull)) continue;
-      const int64_t tj = static_cast<int64_t>(blk) * TB + j;
-      visit(p.kl + tj * p.l_st + hoff, p.vl + tj * p.l_st + hoff);
+  const int hk = blockIdx.y;
+  const int rows_hk = p.num_tokens * p.G;  // rows of this kv head
+  const int row0 = blockIdx.x * kF32Rows;
+
+  // ---- Q rows of the CTA, pre-scaled (rows past the end are zero) ----
+  for (int e = threadIdx.x; e < kF32Rows * D; e += kF32Threads) {
+    const int i = e / D, d = e - (e / D) * D;
+    const int r = row0 + i;
+    float x = 0.f;
+    if (r < rows_hk) {
+      const int tok = r / p.G, hq = hk * p.G + (r - (r / p.G) * p.G);
+      x = p.q[static_cast<int64_t>(tok) * p.q_st + static_cast<int64_t>(hq) * p.q_sh + d] * p.scale;
     }
+    Qs[e] = x;
   }
-  // this part's state: normalised output and base-2 LSE
-  float lse2 = (l > 0.f) ? (m + logf(l)) * kLog2e : -INFINITY;
-  const float inv = (l > 0.f) ? 1.f / l : 0.f;
+
+  // ---- the key tiles: prefix keys, then the block tokens of the CTA's blocks ----
+  const int r_last = min(row0 + kF32Rows, rows_hk) - 1;
+  const int tok_first = row0 / p.G, tok_last = r_last / p.G;
+  const int TB = p.block_len;
+  const int n_pre = p.kp ? p.P - p.kv_start : 0;
+  const int loc0 = p.kl ? (tok_first / TB) * TB : 0;
+  const int loc1 = p.kl ? min((tok_last / TB + 1) * TB, p.num_tokens) : 0;
+  const int t_pre = (n_pre + kF32Keys - 1) / kF32Keys;
+  const int t_all = t_pre + (loc1 - loc0 + kF32Keys - 1) / kF32Keys;
+
+  // stage tile t (K rows at stride KS, V rows at stride D); keys past the end
+  // load a valid key instead (finite values; their P is 0)
+  auto stage = [&](int t, int buf) {
+    float* Kd = sm + S::kQ + buf * S::kStage;
+    float* Vd = Kd + S::kK;
+    const float *kb, *vb;
+    int64_t st, first;
+    int n;
+    if (t < t_pre) {
+      kb = p.kp; vb = p.vp; st = p.p_st;
+      first = p.kv_start + static_cast<int64_t>(t) * kF32Keys;
+      n = min(kF32Keys, p.P - static_cast<int>(first));
+      kb += static_cast<int64_t>(hk) * p.p_sh;
+      vb += static_cast<int64_t>(hk) * p.p_sh;
+    } else {
+      kb = p.kl; vb = p.vl; st = p.l_st;
+      first = loc0 + static_cast<int64_t>(t - t_pre) * kF32Keys;
+      n = min(kF32Keys, loc1 - static_cast<int>(first));
+      kb += static_cast<int64_t>(hk) * p.l_sh;
+      vb += static_cast<int64_t>(hk) * p.l_sh;
+    }
+    constexpr int CH = D / 4;  // 16-byte chunks per row
+    for (int e = threadIdx.x; e < kF32Keys * CH; e += kF32Threads) {
+      const int j = e / CH, c = e - (e / CH) * CH;
+      const int64_t key = first + min(j, n - 1);
+      const float* ks = kb + key * st + 4 * c;
+      const float* vs = vb + key * st + 4 * c;
+      if (aligned) {
+        cp_async16(Kd + j * S::KS + 4 * c, ks);
+        cp_async16(Vd + j * D + 4 * c, vs);
+      } else {
 #pragma unroll
-  for (int k = 0; k < DW; ++k) acc[k] *= inv;
-  if (p.prefix_out) {
-    // merge_state_in_place((prefix_out, prefix_lse), (acc, lse2)), base 2
-    const float lp = p.prefix_lse[static_cast<int64_t>(tok) * p.pl_st + hq];
-    const float M = fmaxf(lp, lse2);
-    const float wa = (lp == -INFINITY) ? 0.f : exp2f(lp - M);
-    const float wb = (lse2 == -INFINITY) ? 0.f : exp2f(lse2 - M);
-    const float den = wa + wb;
-    const float* po = p.prefix_out + static_cast<int64_t>(tok) * p.po_st +
-                      static_cast<int64_t>(hq) * p.po_sh;
+        for (int w = 0; w < 4; ++w) {
+          Kd[j * S::KS + 4 * c + w] = ks[w];
+          Vd[j * D + 4 * c + w] = vs[w];
+        }
+      }
+    }
+    cp_async_commit();
+  };
+
+  // per row of the warp: token, its block / position, allowed local keys
+  int tok_i[4], blk_i[4];
+  uint64_t allow_i[4];
+  bool live_i[4];
 #pragma unroll
-    for (int k = 0; k < DW; ++k)
-      acc[k] = den > 0.f ? (wa * po[lane + 32 * k] + wb * acc[k]) / den : 0.f;
-    lse2 = den > 0.f ? M + log2f(den) : -INFINITY;
+  for (int i = 0; i < 4; ++i) {
+    const int r = row0 + warp * 4 + i;
+    live_i[i] = r < rows_hk;
+    const int tok = live_i[i] ? r / p.G : 0;
+    tok_i[i] = tok;
+    blk_i[i] = tok / TB;
+    const int tt = tok - (tok / TB) * TB;
+    uint64_t a = ~0ull;
+    if (p.mask_mode == D2SD_MASK_CAUSAL) a = (tt >= 63) ? ~0ull : ((2ull << tt) - 1ull);
+    else if (p.mask_mode == D2SD_MASK_CUSTOM && p.kl && live_i[i]) a = p.custom_mask[tok];
+    allow_i[i] = a;
   }
-  float factor = 1.f;
-  if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
-    const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse2 * kLn2 : lse2) - p.sinks[hq];
-    factor = 1.f / (1.f + expf(-x));
-  }
-  float* orow = p.out + static_cast<int64_t>(tok) * p.o_st + static_cast<int64_t>(hq) * p.o_sh;
+  float m_i[4], l_i[4], acc[4][DW];
 #pragma unroll
-  for (int k = 0; k < DW; ++k) orow[lane + 32 * k] = acc[k] * factor;
-  if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(tok) * p.lse_st + hq] = lse2;
+  for (int i = 0; i < 4; ++i) {
+    m_i[i] = -INFINITY;
+    l_i[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < DW; ++c) acc[i][c] = 0.f;
+  }
+
+  if (t_all > 0) stage(0, 0);
+  for (int t = 0; t < t_all; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < t_all) {
+      stage(t + 1, buf ^ 1);  // the next tile's copies run during this tile
+      cp_async_wait_1();
+    } else {
+      cp_async_wait_0();
+    }
+    __syncthreads();  // tile t (and, at t = 0, Q) visible to every warp
+    const float* Kt = sm + S::kQ + buf * S::kStage;
+    const float* Vt = Kt + S::kK;
+    // scores of the warp's 4 rows against key `lane`
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* kr = Kt + lane * S::KS;
+    const float* q0 = Qs + (warp * 4) * D;
+#pragma unroll 8
+    for (int d = 0; d < D; d += 4) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 q4 = *reinterpret_cast<const float4*>(q0 + i * D + d);
+        s[i] = fmaf(q4.x, k4.x, s[i]);
+        s[i] = fmaf(q4.y, k4.y, s[i]);
+        s[i] = fmaf(q4.z, k4.z, s[i]);
+        s[i] = fmaf(q4.w, k4.w, s[i]);
+      }
+    }
+    // which (row, key) pairs count
+    bool valid[4];
+    if (t < t_pre) {
+      const bool in = t * kF32Keys + lane < n_pre;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) valid[i] = in && live_i[i];
+    } else {
+      const int key = loc0 + (t - t_pre) * kF32Keys + lane;
+      const int kb = key / TB, kt = key - (key / TB) * TB;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        valid[i] = live_i[i] && key < loc1 && kb == blk_i[i] && ((allow_i[i] >> kt) & 1ull);
+    }
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float tmax = valid[i] ? s[i] : -INFINITY;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mn = fmaxf(m_i[i], tmax);
+      const float alpha = (m_i[i] == -INFINITY) ? 0.f : expf(m_i[i] - mn);
+      pr[i] = valid[i] ? expf(s[i] - mn) : 0.f;
+      float ps = pr[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      l_i[i] = fmaf(l_i[i], alpha, ps);
+#pragma unroll
+      for (int c = 0; c < DW; ++c) acc[i][c] *= alpha;
+      m_i[i] = mn;
+    }
+    // P.V: lane holds dims lane + 32 c
+#pragma unroll 4
+    for (int j = 0; j < kF32Keys; ++j) {
+      float vv[DW];
+#pragma unroll
+      for (int c = 0; c < DW; ++c) vv[c] = Vt[j * D + lane + 32 * c];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float pj = __shfl_sync(0xffffffffu, pr[i], j);
+#pragma unroll
+        for (int c = 0; c < DW; ++c) acc[i][c] = fmaf(pj, vv[c], acc[i][c]);
+      }
+    }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
+  }
+
+  // ---- per row: normalise, merge with a dense prefix state, sinks, store ----
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (!live_i[i]) continue;
+    const int r = row0 + warp * 4 + i;
+    const int tok = tok_i[i], hq = hk * p.G + (r - (r / p.G) * p.G);
+    const float l = l_i[i], m = m_i[i];
+    float lse2 = (l > 0.f) ? (m + logf(l)) * kLog2e : -INFINITY;
+    const float inv = (l > 0.f) ? 1.f / l : 0.f;
+    float o[DW];
+#pragma unroll
+    for (int c = 0; c < DW; ++c) o[c] = acc[i][c] * inv;
+    if (p.prefix_out) {
+      // merge_state_in_place((prefix_out, prefix_lse), (o, lse2)), base 2
+      const float lp = p.prefix_lse[static_cast<int64_t>(tok) * p.pl_st + hq];
+      const float M = fmaxf(lp, lse2);
+      const float wa = (lp == -INFINITY) ? 0.f : exp2f(lp - M);
+      const float wb = (lse2 == -INFINITY) ? 0.f : exp2f(lse2 - M);
+      const float den = wa + wb;
+      const float* po = p.prefix_out + static_cast<int64_t>(tok) * p.po_st +
+                        static_cast<int64_t>(hq) * p.po_sh;
+#pragma unroll
+      for (int c = 0; c < DW; ++c)
+        o[c] = den > 0.f ? (wa * po[lane + 32 * c] + wb * o[c]) / den : 0.f;
+      lse2 = den > 0.f ? M + log2f(den) : -INFINITY;
+    }
+    float factor = 1.f;
+    if (p.sinks && p.sink_mode != D2SD_SINK_NONE) {
+      const float x = (p.sink_mode == D2SD_SINK_EXACT ? lse2 * kLn2 : lse2) - p.sinks[hq];
+      factor = 1.f / (1.f + expf(-x));
+    }
+    float* orow = p.out + static_cast<int64_t>(tok) * p.o_st + static_cast<int64_t>(hq) * p.o_sh;
+#pragma unroll
+    for (int c = 0; c < DW; ++c) orow[lane + 32 * c] = o[c] * factor;
+    if (lane == 0 && p.lse) p.lse[static_cast<int64_t>(tok) * p.lse_st + hq] = lse2;
+  }
+}
+
+template <int D>
+int launch_f32(const F32Params& prm, int num_kv_heads, cudaStream_t st) {
+  using S = F32Smem<D>;
+  static int configured = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    cudaError_t e = cudaFuncSetAttribute(cascade_f32_kernel<D>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(S::kBytes));
+    if (e != cudaSuccess)
+      return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    configured = dev;
+  }
+  // 16-byte copies need 16-byte aligned rows
+  auto al = [](const void* ptr, int64_t a, int64_t b) {
+    return ptr == nullptr ||
+           ((reinterpret_cast<uintptr_t>(ptr) & 15u) == 0 && a % 4 == 0 && b % 4 == 0);
+  };
+  const int aligned = al(prm.kp, prm.p_st, prm.p_sh) && al(prm.vp, prm.p_st, prm.p_sh) &&
+                      al(prm.kl, prm.l_st, prm.l_sh) && al(prm.vl, prm.l_st, prm.l_sh);
+  const int64_t rows_hk = static_cast<int64_t>(prm.num_tokens) * prm.G;
+  const dim3 grid(static_cast<unsigned>((rows_hk + kF32Rows - 1) / kF32Rows),
+                  static_cast<unsigned>(num_kv_heads));
+  cascade_f32_kernel<D><<<grid, kF32Threads, S::kBytes, st>>>(prm, aligned);
+  return check_launch("cascade_f32_kernel");
 }
 
 }  // namespace
@@ -187,11 +375,10 @@ extern "C" int d2sd_cascade_attention_f32(
   prm.Hq = num_qo_heads;
   prm.G = num_qo_heads / num_kv_heads;
   prm.scale = sm_scale;
-  const int64_t rows = n * num_qo_heads;
-  const dim3 grid(static_cast<unsigned>((rows + 3) / 4));
+  if (n * (num_qo_heads / num_kv_heads) > INT32_MAX)
+    return fail(D2SD_ERR_UNSUPPORTED, "d2sd_cascade_attention_f32: too many rows");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (head_dim == 128) cascade_f32_kernel<4><<<grid, 128, 0, st>>>(prm);
-  else if (head_dim == 64) cascade_f32_kernel<2><<<grid, 128, 0, st>>>(prm);
-  else cascade_f32_kernel<1><<<grid, 128, 0, st>>>(prm);
-  return check_launch("cascade_f32_kernel");
+  if (head_dim == 128) return launch_f32<128>(prm, num_kv_heads, st);
+  if (head_dim == 64) return launch_f32<64>(prm, num_kv_heads, st);
+  return launch_f32<32>(prm, num_kv_heads, st);
 }

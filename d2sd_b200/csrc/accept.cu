@@ -340,6 +340,9 @@ __global__ void __launch_bounds__(kThreads, 3)  // the grid is 3 CTAs per SM
   const int TB = sh.TB, B = sh.B;
   const int bt = B * TB;
   const int rows = sh.R * bt;
+  // launched with programmatic serialisation: the logits and ids may be
+  // written by the previous kernel of the stream
+  grid_dep_wait();
   const int64_t u_begin = static_cast<int64_t>(blockIdx.x) * pt.W;
   const int64_t u_end = u_begin + pt.W < pt.total ? u_begin + pt.W : pt.total;
   for (int64_t u = u_begin; u < u_end;) {
@@ -378,6 +381,9 @@ __global__ void __launch_bounds__(kThreads, 3)  // the grid is 3 CTAs per SM
   // last CTA's thread 0 acquires them all and the barrier hands them on
   if (threadIdx.x == 0) last = atom_add_acq_rel_gpu(ws.ticket, 1u) == gridDim.x - 1;
   __syncthreads();
+  // the next kernel (the commit) may set itself up once every CTA is here; it
+  // waits for this whole grid before it reads the results
+  grid_dep_launch();
   if (!last) return;
 
   // ---- last CTA: per-row argmax over the (at most a few) CTA segments of the
@@ -579,13 +585,12 @@ int launch_accept(const void* logits, const Shape& sh, const int64_t* ids, int32
       return fail(D2SD_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     configured[vec] = dev;
   }
+  const T* lg = static_cast<const T*>(logits);
   if (vec)
-    accept_kernel<T, true><<<grid, kThreads, smem, stream>>>(static_cast<const T*>(logits), sh, ids,
-                                                          result, acc_ids, argmax_out, ws, pt, ax);
-  else
-    accept_kernel<T, false><<<grid, kThreads, smem, stream>>>(static_cast<const T*>(logits), sh, ids,
-                                                           result, acc_ids, argmax_out, ws, pt, ax);
-  return check_launch("accept_kernel");
+    return launch_pdl(accept_kernel<T, true>, dim3(grid), dim3(kThreads), smem, stream,
+                      "accept_kernel", lg, sh, ids, result, acc_ids, argmax_out, ws, pt, ax);
+  return launch_pdl(accept_kernel<T, false>, dim3(grid), dim3(kThreads), smem, stream,
+                    "accept_kernel", lg, sh, ids, result, acc_ids, argmax_out, ws, pt, ax);
 }
 
 int accept_dispatch(const void* logits, int32_t dtype, const Shape& sh, const int64_t* ids,

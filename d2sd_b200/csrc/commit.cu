@@ -54,6 +54,9 @@ struct CommitArgs {
 
 __global__ void __launch_bounds__(kThreads)
     commit_kernel(const CommitArgs a, const HiddenGather hg) {
+  // launched with programmatic serialisation: everything below reads the
+  // acceptance result of the previous kernel
+  grid_dep_wait();
   const int64_t per_req = static_cast<int64_t>(a.L) * 2 * a.Hk * a.vec_per_row;
   const int64_t total = per_req * a.R;
   const int64_t total_h = static_cast<int64_t>(hg.n) * hg.vec_per_row;
@@ -100,24 +103,29 @@ __global__ void __launch_bounds__(kThreads)
                          ((r * a.n_sr + branch * a.n_sb + h * a.n_sh) * a.elem_bytes + vv * 16);
     uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(a.layer_ptrs[4 * l + 2 + kv]));
     for (int t0 = 0; t0 < acc; t0 += kUnroll) {
+      // the rows and their pages are loaded before any store (a store through
+      // the byte pointer could alias a later load and would serialise them)
       uint4 v[kUnroll];
+      int64_t page[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-        if (t0 + u < acc)
-          v[u] = *reinterpret_cast<const uint4*>(src + (t0 + u) * a.n_st * a.elem_bytes);
+      for (int u = 0; u < kUnroll; ++u) {
+        if (t0 + u < acc) {
+          v[u] = __ldg(reinterpret_cast<const uint4*>(src + (t0 + u) * a.n_st * a.elem_bytes));
+          const int64_t pidx = (len + t0 + u) / a.page_size;
+          page[u] = pt ? static_cast<int64_t>(__ldg(pt + pidx)) : pidx;
+        }
+      }
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         if (t0 + u >= acc) break;
         const int64_t pos = len + t0 + u;
-        const int64_t pidx = pos / a.page_size;
-        const int64_t page = pt ? static_cast<int64_t>(pt[pidx]) : pidx;
         const int s = static_cast<int>(pos % a.page_size);
         // UMMA pages: 16-byte chunk vv of row s sits in core matrix (s/8, vv), row s%8
         const int64_t in_page =
             a.umma_pages ? ((static_cast<int64_t>(s / 8) * a.vec_per_row + vv) * 64 + (s % 8) * 8)
                          : static_cast<int64_t>(s) * a.c_ss;
         const int64_t d_off =
-            (page * a.c_sp + h * a.c_sh + in_page) * a.elem_bytes + (a.umma_pages ? 0 : vv * 16);
+            (page[u] * a.c_sp + h * a.c_sh + in_page) * a.elem_bytes + (a.umma_pages ? 0 : vv * 16);
         *reinterpret_cast<uint4*>(dst + d_off) = v[u];
       }
     }
@@ -154,9 +162,8 @@ int commit_impl(CommitArgs a, int32_t head_dim, int32_t cache_format, const Hidd
   int64_t blocks = (total + kThreads - 1) / kThreads;
   const int64_t max_blocks = static_cast<int64_t>(current_sm_count()) * 8;
   if (blocks > max_blocks) blocks = max_blocks;
-  commit_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      a, hg);
-  return check_launch("commit_kernel");
+  return launch_pdl(commit_kernel, dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0,
+                    static_cast<cudaStream_t>(stream), "commit_kernel", a, hg);
 }
 
 CommitArgs single_args(const void* const* layer_ptrs, int32_t num_layers, int32_t num_kv_heads,

@@ -637,13 +637,22 @@ __global__ void merge_state_kernel(T* v, int64_t v_st, int64_t v_sh, float* s, i
 namespace d2sd {
 namespace {
 // Rows per CTA: a whole 128-row tile when tiles are plenty (two CTAs fit an
-// SM), else 64 .. 8 rows -- more CTAs, and more lane groups per row -- when few
+// SM), else fewer rows -- more CTAs, and more lane groups per row -- when few
 // tiles would leave SMs idle (KV-head sharding over several GPUs leaves each
 // rank few heads, and each query tile then has many partial slots to merge).
+// RP halves while the doubled CTA count still fits one CTA per SM, and while
+// RP is above 32 with fewer CTAs than SMs. Measured on config 3's per-rank
+// shapes ((a)+(b) per layer, one-rank exchange): 64 tiles -> RP 32 (256 CTAs;
+// 128 CTAs cost 2 us more), 32 tiles -> RP 32 (128 CTAs; 256 cost 1.6 us
+// more), 16 tiles -> RP 16, 8 tiles -> RP 8.
 int rows_per_cta(int64_t tiles) {
-  const int64_t target = current_sm_count();
+  const int64_t sms = current_sm_count();
   int rp = kTileRows;
-  while (rp > 8 && tiles * (kTileRows / rp) < target) rp /= 2;
+  while (rp > 8) {
+    const int64_t ctas = tiles * (kTileRows / rp);
+    if (ctas * 2 <= sms || (rp > 32 && ctas < sms)) rp /= 2;
+    else break;
+  }
   return rp;
 }
 

@@ -139,8 +139,23 @@ __device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
 }
 
 // pairs of each 32-key chunk whose exponentials go to exp2_poly2 (bit e = pair
-// e): one in eight, measured best on cfg3 (one in four to one in two was slower)
+// e): one in eight, measured best on cfg3 (one in four to one in two was slower,
+// at D 64 as at D 128)
 constexpr uint32_t kPolyPairs = 0x8080u;
+
+// P is rounded to bf16 by truncation: one byte permute per pair, where rounding
+// to nearest costs two more integer adds on the softmax's critical issue path
+// (3% of kernel (a)'s time on cfg3). Truncation drops the bits below bf16's
+// 7-bit fraction, on average half a last place: 2^-8 / m of a weight with
+// mantissa m in [1, 2); over log-uniform mantissas (softmax weights span many
+// octaves) E[1/m] = 1 / (2 ln 2), a mean loss of 0.2818%. The row sum l comes
+// from the f32 weights, so that mean loss is divided out of O in the epilogue;
+// what remains is zero-mean, between -0.49% and +0.28% of a weight (round to
+// nearest: +-0.39%), and averages out over a row's many weights.
+constexpr float kTruncBias = 1.0f / (1.0f - 0.002818f);
+__device__ __forceinline__ uint32_t pack_bf16x2_trunc(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+}
 
 // Producer warp. The page indices of a KV tile are fetched by the whole warp
 // (lane b reads page b of the tile) one tile ahead of their use, so no copy
@@ -467,7 +482,7 @@ __device__ void softmax_role(const PrefixParams& p, uint8_t* smem, uint64_t* bar
               p1 = fast_exp2(x1);
             }
             acc2[e & 3] = f2_add(acc2[e & 3], f2_pack(p0, p1));
-            pk[e] = pack_bf16x2_int(p0, p1);
+            pk[e] = pack_bf16x2_trunc(p0, p1);
           }
           tmem_st16(lane_base + s_col(i) + c * 16, pk);
           release_half(c);
@@ -488,7 +503,7 @@ __device__ void softmax_role(const PrefixParams& p, uint8_t* smem, uint64_t* bar
             const float p1 = fast_exp2(fmaf(__uint_as_float(s[c * 32 + 2 * e + 1]), sl2, neg_m));
             sm[(2 * e) & 7] += p0;
             sm[(2 * e + 1) & 7] += p1;
-            pk[e] = pack_bf16x2(p0, p1);
+            pk[e] = pack_bf16x2_trunc(p0, p1);
           }
           tmem_st16(lane_base + s_col(i) + c * 16, pk);
           release_half(c);
@@ -525,8 +540,8 @@ __device__ void softmax_role(const PrefixParams& p, uint8_t* smem, uint64_t* bar
     tc_fence_after();
     if (slot >= 0) {
       // normalised O of this row in bf16 (the precision FlashInfer hands to its
-      // merge), base-2 LSE in fp32
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      // merge), base-2 LSE in fp32; the mean truncation loss of P divided out
+      const float inv = l_run > 0.f ? kTruncBias / l_run : 0.f;
       uint8_t* sb = reinterpret_cast<uint8_t*>(p.partial) + static_cast<int64_t>(slot) * slot_bytes(D);
       // Each thread holds its own row; storing it directly would scatter every
       // warp store over 32 rows. So each 64-column panel goes through this

@@ -139,9 +139,12 @@ __device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
 }
 
 // pairs of each 32-key chunk whose exponentials go to exp2_poly2 (bit e = pair
-// e): one in eight, measured best on cfg3 (one in four to one in two was slower,
-// at D 64 as at D 128)
-constexpr uint32_t kPolyPairs = 0x8080u;
+// e): the last pair, one in sixteen. Measured on cfg3 with the truncating pack
+// below, kernel (a) per launch: none 119.5 us, pair 15 116 us, pair 0 117 us,
+// pair 8 120 us, pairs 7 and 15 120 us, one in thirty-two 116 us; one in four
+// or more is slower still (the softmax is bound by instruction issue as much as
+// by the ex2 unit), at D 64 as at D 128.
+constexpr uint32_t kPolyPairs = 0x8000u;
 
 // P is rounded to bf16 by truncation: one byte permute per pair, where rounding
 // to nearest costs two more integer adds on the softmax's critical issue path

@@ -158,3 +158,20 @@ def test_plan_groups_share_kv_stream(lib):
         for k in range(1, 4):
             assert np.array_equal(lists[k][:, [0, 1, 4, 5]], lists[0][:, [0, 1, 4, 5]])
             assert np.all(lists[k][:, 2] == lists[0][:, 2] + 2 * k)
+
+
+def test_truncation_bias_constant():
+    """The mean relative loss of truncating f32 softmax weights to bf16 (the
+    constant kernel (a) divides out of O) for weights spread over many octaves:
+    half a last place, 2^-8 / m for mantissa m, averaged over log-uniform m,
+    2^-8 / (2 ln 2) = 0.2818%."""
+    import re
+    from pathlib import Path
+    src = (Path(__file__).resolve().parents[1] / "d2sd_b200" / "csrc" / "prefix_attn.cu").read_text()
+    c = float(re.search(r"kTruncBias = 1\.0f / \(1\.0f - ([0-9.]+)f\)", src).group(1))
+    rng = np.random.default_rng(0)
+    p = np.exp2(rng.uniform(-20.0, 8.0, 2_000_000)).astype(np.float32)
+    tr = (p.view(np.uint32) & np.uint32(0xFFFF0000)).view(np.float32)
+    loss = 1.0 - float(np.mean(tr / p))
+    assert abs(loss - c) < 2e-5, (loss, c)
+    assert abs(c - 2.0 ** -8 / (2.0 * np.log(2.0))) < 1e-5

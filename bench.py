@@ -1432,7 +1432,16 @@ def bench_cfg2(ctx: Ctx) -> dict:
         prefix = torch.randint(0, V, (1, P), generator=g, device=dev)
         cache = model(prefix, use_cache=True).past_key_values
     ids = torch.randint(0, V, (B, T), generator=g, device=dev)
+    ids[:, 0] = ids[0, 0]  # the block's anchor token, shared by the branches
     pos = torch.arange(P, P + T, device=dev).view(1, T)
+    # drafts of the survey's p = 0.7 draft model: position by position, a
+    # branch's token t is the target's argmax at t - 1 with probability 0.7
+    # (the forward is causal inside a branch, so fixing t leaves t - 1 as it is)
+    with torch.no_grad():
+        for t in range(1, T):
+            lg, _, _ = cascade_verify_forward(model, ids, pos, cache, True)
+            keep = torch.rand(B, generator=g, device=dev) < 0.7
+            ids[:, t] = torch.where(keep, lg[:, t - 1].float().argmax(-1), ids[:, t])
     ver = d.BatchVerifier(1, B, T, V, dev)
 
     def step(_i, input_ids=ids):
@@ -1442,6 +1451,7 @@ def bench_cfg2(ctx: Ctx) -> dict:
     ms_total, clocks, graph = timed_steps(ctx, lambda: step(0), a.steps, a.warmup)
     del graph
     ms = ms_total / a.steps
+    acc_len = int(ver.result[0, 0].item())
     # the attention kernels alone on the same shapes (36 x (a)+(b)) for the share
     Hq, Hk, D = c["qo_heads"], c["kv_heads"], c["head_dim"]
     qa = torch.randn(B, T, Hq, D, device=dev, dtype=torch.bfloat16)
@@ -1464,6 +1474,8 @@ def bench_cfg2(ctx: Ctx) -> dict:
     out = {
         "metric": "verified tokens/s", "unit": "tokens/s", "value": B * T / (ms / 1e3),
         "ms_per_step": ms, "n_gpus": 1, "scaling": "strong", "clocks": clocks,
+        "committed_tokens_per_s": acc_len / (ms / 1e3), "acceptance_length": acc_len,
+        "drafts": "each branch's token t = the target's argmax at t - 1 with probability 0.7",
         "timing": "the step captured once into a CUDA graph and replayed (the HF reference path below runs eagerly, as the reference does)",
         "workload": (f"BASELINE config 2: Qwen3-8B architecture, random init (std 0.02), bf16, "
                      f"{c['layers']} layers, hidden {c['hidden']}, {Hq}/{Hk} heads, D {D}, vocab "
@@ -1482,7 +1494,9 @@ def bench_cfg2(ctx: Ctx) -> dict:
                                   "what": ("the reference's plain_verify_forward (HF sdpa) "
                                            "branch by branch with a cache crop, same GPU and "
                                            "weights")},
-        "gpu_launches": None,
+        # this library's kernels per step: QK-norm + RoPE, (a) and (b) per layer,
+        # then the acceptance (the projections, MLP and lm_head are cuBLAS)
+        "gpu_launches": a.steps * (3 * c["layers"] + 1),
     }
     if not a.no_e2e:
         h_ids = ids.cpu().pin_memory()

@@ -97,3 +97,51 @@ def test_kv_head_sharded_equals_unsharded(world):
     from oracle import attention as AT
     ref, _ = AT.cascade_attention(q, kn, vn, kp, vp)
     np.testing.assert_allclose(full, ref.reshape(B * T, Hq, D), atol=1e-5)
+
+
+def test_vocab_ranges_partition_the_vocabulary():
+    for V in (151936, 201088, 1000, 7):
+        for world in (1, 2, 3, 4, 8):
+            cols = [S.vocab_range(V, world, r) for r in range(world)]
+            assert cols[0][0] == 0 and cols[-1][1] == V
+            assert all(cols[r][1] == cols[r + 1][0] for r in range(world - 1))
+            widths = [b - a for a, b in cols]
+            assert max(widths) - min(widths) <= 1
+
+
+def _better(va, ia, vb, ib):
+    """The total order kernel (c) keeps: NaN above every number, larger value
+    first, equal values -> smaller index (accept.cu, better())."""
+    na, nb = va != va, vb != vb
+    if na or nb:
+        return ia < ib if (na and nb) else na
+    if va != vb:
+        return va > vb
+    return ia < ib
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_sharded_argmax_combine_equals_torch_argmax(world):
+    """Vocabulary-sharded acceptance: each rank's (max, first index) over its
+    slice, combined over the ranks in rank order with the kernel's order, is
+    torch.argmax of the whole row -- ties across a slice boundary and NaNs
+    included."""
+    g = torch.Generator().manual_seed(world)
+    V = 997
+    rows = torch.randn(64, V, generator=g).to(torch.bfloat16).float()
+    rows[1, [10, 500, 900]] = 9.0                       # ties in three slices
+    rows[2, :] = -float("inf")                          # all -inf: index 0
+    rows[3, [700, 20]] = float("nan")                   # first NaN wins
+    lo, hi = S.vocab_range(V, world, 1)
+    rows[4, [lo - 1, lo]] = 7.5                         # tie across a boundary
+    for r in range(rows.shape[0]):
+        best_v, best_i = -float("inf"), None
+        for k in range(world):
+            a, b = S.vocab_range(V, world, k)
+            sl = rows[r, a:b]
+            if b > a:
+                i = int(torch.argmax(sl))              # the slice's first maximal index
+                v, i = float(sl[i]), a + i
+                if best_i is None or _better(v, i, best_v, best_i):
+                    best_v, best_i = v, i
+        assert best_i == int(torch.argmax(rows[r])), r

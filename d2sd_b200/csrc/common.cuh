@@ -459,15 +459,5 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Two finite non-negative floats to packed bf16x2 (lo in the low half) on the
-// integer pipe: add half a bf16 unit in the last place to each bit pattern and
-// keep the high halves (round to nearest, ties away from zero). On sm_100 the
-// f32 -> bf16x2 conversion shares the issue pipe of ex2; two integer adds and a
-// byte permute leave that pipe to the exponentials.
-__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
-  const uint32_t a = __float_as_uint(lo) + 0x8000u;
-  const uint32_t b = __float_as_uint(hi) + 0x8000u;
-  return __byte_perm(a, b, 0x7632);
-}
 
 }  // namespace d2sd
